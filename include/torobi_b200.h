@@ -1,0 +1,194 @@
+/*
+ * torobi_b200 -- C ABI of the B200 (sm_100a) backend for Torobi's
+ * quantized-weight QLoRA path.
+ *
+ * The reference engine (takahashim/torobi, Rust) reaches its device through
+ * mlx-c, whose convention this ABI keeps (docs/vendoring.md:291-297): every
+ * call returns an int status (0 = ok), borrows its inputs, writes into
+ * caller-owned outputs, and takes the stream it runs on.  Nothing here
+ * allocates device memory in the hot calls; all buffers are the caller's.
+ *
+ * Data types on this boundary
+ *   bf16      16-bit brain float, passed as raw device pointers
+ *   codes     uint32, 32/bits codes per word packed low bits first along the
+ *             last axis of the [rows, cols] weight (MLX affine layout)
+ *   scales,
+ *   biases    bf16 [rows, cols / group_size]; w = scale * q + bias
+ *   f32       float (LoRA master parameters, gradients, optimizer moments)
+ * Every device pointer must be 16-byte aligned; row pitches are the dense
+ * row widths given.
+ *
+ * Streams are cudaStream_t passed as void* (NULL = legacy default stream).
+ */
+#ifndef TOROBI_B200_H
+#define TOROBI_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TQ_OK 0
+#define TQ_ERR_INVALID 1     /* a shape or argument the op does not accept   */
+#define TQ_ERR_UNSUPPORTED 2 /* bits / group_size / rank outside the set     */
+#define TQ_ERR_MISALIGNED 3  /* a pointer or row pitch breaks 16-byte rule  */
+#define TQ_ERR_TIMEOUT 4     /* a device-side wait ran out (see tq_device_status) */
+#define TQ_ERR_CUDA 5        /* a CUDA runtime call failed                   */
+#define TQ_ERR_NCCL 6        /* an NCCL call failed                          */
+
+#define TQ_DTYPE_F32 0
+#define TQ_DTYPE_BF16 1
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int tq_version(void);
+
+/*
+ * Message of the last failing call on this host thread ("" if none).
+ * Replaces the message mlx-c hands to the installed error handler
+ * (engine/src/mlxc/error.rs:1-80).
+ */
+const char* tq_last_error(void);
+
+/*
+ * Reads (and with clear != 0 resets) the device status word of the current
+ * device: bit 1 = a kernel's bounded wait ran out.  Synchronizes the device.
+ * Returns TQ_OK, or TQ_ERR_TIMEOUT when the word is non-zero.
+ */
+int tq_device_status(int* status_out, int clear);
+
+/* ---------------------------------------------------------------- packing */
+
+/*
+ * MLX affine quantization of a bf16 matrix w [rows, cols] along cols:
+ * codes [rows, cols*bits/32] u32, scales/biases [rows, cols/group_size] bf16.
+ * bits in {4, 8}; group_size in {32, 64, 128}; cols % group_size == 0.
+ * Replaces mlx_quantize (MLX 0.32.2), which the reference never binds
+ * (engine/src/mlxc/ops.rs:91-130 has no quantize); it runs where imported
+ * weights are converted to their declared dtype (engine/src/plan.rs:499).
+ */
+int tq_quantize(const void* w, int64_t rows, int64_t cols, int group_size, int bits, void* codes,
+                void* scales, void* biases, void* stream);
+
+/*
+ * Inverse of tq_quantize: w [rows, cols] bf16 = RNE(scale * q + bias).
+ * Replaces mlx_dequantize (MLX 0.32.2; unbound in the reference).
+ */
+int tq_dequantize(const void* codes, const void* scales, const void* biases, int64_t rows,
+                  int64_t cols, int group_size, int bits, void* w, void* stream);
+
+/* ----------------------------------------------------------- the GEMM ---- */
+
+/*
+ * quantized_matmul with MLX's argument meaning, W the quantized
+ * [w_rows, w_cols] matrix packed along w_cols:
+ *   transpose != 0:  y[m, w_rows] = x[m, w_cols] . W^T   (linear forward)
+ *   transpose == 0:  y[m, w_cols] = x[m, w_rows] . W     (its VJP wrt x)
+ * bf16 in, f32 accumulation on the tensor cores, bf16 out.
+ * Requires w_rows % 8 == 0 and w_cols % group_size == 0.
+ * Replaces Op::Matmul -> mlx_matmul (engine/src/interp.rs:270,
+ * engine/src/mlxc/ops.rs:108) for the frozen base weight of a linear
+ * (lib/torobi/dsl/layers.rb:22), and the matmul VJP MLX derives for it
+ * (engine/src/executor.rs:163-191).
+ */
+int tq_quantized_matmul(const void* x, const void* codes, const void* scales, const void* biases,
+                        int64_t m, int64_t w_rows, int64_t w_cols, int transpose, int group_size,
+                        int bits, void* y, void* stream);
+
+/*
+ * The adapted linear in one kernel: quantized_matmul (as above) plus an
+ * optional bias and the LoRA up-projection accumulated into the same
+ * tensor-memory accumulator before the single rounding to bf16:
+ *   transpose != 0:  y = x . W^T + bias + lora_down . lora_up^T
+ *                    lora_up = LoRA B [w_rows, rank]
+ *   transpose == 0:  y = x . W + lora_down . lora_up
+ *                    lora_up = LoRA A [rank, w_cols]   (bias must be NULL)
+ * lora_down is the caller's [m, rank] bf16 down-projection, already scaled
+ * by alpha/rank (tq_lora_down).  rank in {8, 16}; lora_up/lora_down NULL
+ * (rank 0) leaves the plain GEMM.
+ * Replaces the node chain matmul, add, matmul, matmul, mul_scalar, add of
+ * lib/torobi/dsl/layers.rb:22-24 and lib/torobi/lora.rb:79-85, dispatched at
+ * engine/src/interp.rs:192,198,247,270.
+ */
+int tq_qlora_matmul(const void* x, const void* codes, const void* scales, const void* biases,
+                    int64_t m, int64_t w_rows, int64_t w_cols, int transpose, int group_size,
+                    int bits, const void* bias, const void* lora_up, const void* lora_down,
+                    int64_t rank, void* y, void* stream);
+
+/* ------------------------------------------------------- LoRA side branch */
+
+/*
+ * Down-projection of the LoRA branch, scaled, on the tensor cores:
+ *   out  [m, rank] bf16 = RNE(scale * x . a^T)
+ *   out_t[rank, ld_t] bf16 = the same values transposed (optional, may be
+ *         NULL); ld_t >= m and ld_t % 8 == 0, columns m.. are left untouched
+ * x bf16 [m, k]; a bf16 [rank, k]; f32 accumulation; rank in {8, 16}.
+ * Forward: a = LoRA A, the `matmul(x, a.transpose)` of lib/torobi/lora.rb:83
+ * with the `* scale` of :84 folded in.  Backward: x = dY and a = B^T, the
+ * `dY . B . scale` partner of the same VJP (engine/src/executor.rs:163-191).
+ * out feeds tq_qlora_matmul; out_t feeds tq_lora_grad.
+ */
+int tq_lora_down(const void* x, const void* a, int64_t m, int64_t k, int64_t rank, float scale,
+                 void* out, void* out_t, int64_t ld_t, void* stream);
+
+/*
+ * LoRA weight gradient on the tensor cores, reduced over the m rows:
+ *   out_layout == 0: g[c, rank] = sum_m x[m, c] * p_t[rank, m]   (dB = dY^T . t)
+ *   out_layout == 1: g[rank, c] = sum_m p_t[rank, m] * x[m, c]   (dA = u^T . x)
+ * x bf16 [m, c] (c % 8 == 0); p_t bf16 [rank, ld_p] (tq_lora_down's out_t,
+ * ld_p >= m, ld_p % 8 == 0); g f32.
+ * accumulate != 0 adds into g (micro-batch accumulation,
+ * engine/src/state.rs:418-449); otherwise g is overwritten.
+ * Replaces the matmul VJPs MLX derives for lib/torobi/lora.rb:83-84
+ * (engine/src/executor.rs:163-191).
+ */
+int tq_lora_grad(const void* x, const void* p_t, int64_t ld_p, int64_t m, int64_t c,
+                 int64_t rank, int out_layout, int accumulate, void* g, void* stream);
+
+/* ---------------------------------------------------------- optimizer ---- */
+
+/*
+ * Sum of squares of n f32 values into *out (device f32); accumulate != 0 adds
+ * to *out.  Building block of the global norm of engine/src/optimizer.rs:64-82.
+ */
+int tq_sumsq(const float* x, int64_t n, float* out, int accumulate, void* stream);
+
+/*
+ * One fused AdamW update over n f32 parameters, following
+ * engine/src/optimizer.rs:305-352: moments, bias correction from step t
+ * (the count after this step), then decoupled weight decay.
+ * The gradient is read as grad * grad_scale (e.g. 1/world_size).
+ * norm_sq (optional, device): sum of squares of the unscaled gradient buffer.
+ *   If it is not finite the update is skipped and params/moments are left as
+ *   they were (engine/src/state.rs:360-370).  If clip > 0 and
+ *   sqrt(norm_sq) * |grad_scale| > clip, the gradient is further scaled by
+ *   clip / that norm (engine/src/state.rs:373-376).
+ * params_bf16 (optional) receives RNE(params) after the update.
+ */
+int tq_adamw(float* params, const float* grads, float* m, float* v, int64_t n, int64_t t,
+             float lr, float beta1, float beta2, float eps, float weight_decay, float grad_scale,
+             const float* norm_sq, float clip, void* params_bf16, void* stream);
+
+/*
+ * dst[cols, rows] bf16 = RNE(src[rows, cols]) transposed: the K-major copy of
+ * LoRA B that the backward down-projection (tq_lora_down with a = B^T) reads.
+ */
+int tq_transpose_to_bf16(const float* src, int64_t rows, int64_t cols, void* dst, void* stream);
+
+/* ------------------------------------------------------ data parallel ---- */
+/*
+ * NCCL communicator for the data-parallel step (no reference counterpart:
+ * distribution is a non-goal there, docs/plan.md:108).  The unique id is
+ * 128 opaque bytes made on rank 0 and shared by the caller.
+ */
+int tq_dp_unique_id(void* id128);
+int tq_dp_comm_init(void** comm, const void* id128, int nranks, int rank);
+int tq_dp_allreduce_sum(void* comm, void* buf, int64_t count, int dtype, void* stream);
+int tq_dp_comm_destroy(void* comm);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TOROBI_B200_H */

@@ -1,0 +1,59 @@
+"""The C ABI without a GPU: the library loads, exports every symbol the
+public header declares, and reports argument errors (checked on the host
+before any CUDA call) with a status and a message."""
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+
+
+def test_library_exports_every_header_symbol():
+    import torobi_b200 as tq
+
+    L = tq.lib()
+    names = tq.header_symbols()
+    assert len(names) >= 16
+    for name in names:
+        assert hasattr(L, name), f"{name} declared in include/torobi_b200.h but not exported"
+    from torobi_b200._lib import SIGNATURES
+
+    assert set(SIGNATURES) == set(names), "ctypes signatures out of step with the header"
+
+
+def test_version_and_empty_error():
+    import torobi_b200 as tq
+
+    assert tq.lib().tq_version() >= 100
+
+
+def test_host_side_argument_errors_need_no_gpu():
+    import torobi_b200 as tq
+    from torobi_b200._lib import TQ_ERR_INVALID, TQ_ERR_UNSUPPORTED
+
+    L = tq.lib()
+    dummy = ctypes.c_void_p(16)
+    rc = L.tq_quantize(dummy, 4, 96, 64, 4, dummy, dummy, dummy, None)
+    assert rc == TQ_ERR_INVALID
+    assert b"divisible" in L.tq_last_error()
+    rc = L.tq_quantize(dummy, 4, 64, 64, 3, dummy, dummy, dummy, None)
+    assert rc == TQ_ERR_UNSUPPORTED and b"bits" in L.tq_last_error()
+    rc = L.tq_quantized_matmul(dummy, dummy, dummy, dummy, 4, 12, 64, 1, 64, 4, dummy, None)
+    assert rc == TQ_ERR_INVALID and b"multiple of 8" in L.tq_last_error()
+    rc = L.tq_qlora_matmul(dummy, dummy, dummy, dummy, 4, 16, 64, 1, 64, 4, None, dummy, dummy, 4,
+                           dummy, None)
+    assert rc == TQ_ERR_UNSUPPORTED and b"rank" in L.tq_last_error()
+    rc = L.tq_adamw(dummy, dummy, dummy, dummy, 10, 0, 0.1, 0.9, 0.999, 1e-8, 0.0, 1.0, None, 0.0,
+                    None, None)
+    assert rc == TQ_ERR_INVALID and b"step count" in L.tq_last_error()
+    rc = L.tq_lora_grad(dummy, dummy, 4, 8, 12, 8, 0, 0, dummy, None)
+    assert rc == TQ_ERR_INVALID and b"multiple of 8" in L.tq_last_error()
+
+
+def test_ops_refuse_cpu_tensors():
+    import torch
+    import torobi_b200 as tq
+
+    w = torch.zeros((8, 64), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        tq.quantize(w, 64, 4)

@@ -1,0 +1,133 @@
+"""Parity of the adapted linear (quantized base + LoRA branch) with the oracle.
+
+The oracle computes the reference graph (lib/torobi/dsl/layers.rb:16-25,
+lib/torobi/lora.rb:79-85) in bf16 with every op rounded, and its VJP.
+Tolerance: max rel err 1e-2 for y, dx, dA and dB.
+"""
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from _util import dev_bf16, dev_u32, host_bf16
+
+TOL = 1e-2
+
+
+def _run_adapted(tq, cuda, x, c, s, b, a, bl, scale, bits, group, bias=None, dy=None):
+    import torch
+
+    X = dev_bf16(x, cuda)
+    A = dev_bf16(a, cuda)
+    B = dev_bf16(bl, cuda)
+    C, S, Bi = dev_u32(c, cuda), dev_bf16(s, cuda), dev_bf16(b, cuda)
+    ts, ts_t = tq.lora_down(X, A, scale)
+    y = tq.qlora_matmul(X, C, S, Bi, True, group, bits,
+                        bias=dev_bf16(bias, cuda) if bias is not None else None,
+                        lora_up=B, lora_down=ts)
+    out = {"y": y.float().cpu().numpy()}
+    if dy is not None:
+        DY = dev_bf16(dy, cuda)
+        bt = tq.transpose_to_bf16(B.float())
+        us, us_t = tq.lora_down(DY, bt, scale)
+        dx = tq.qlora_matmul(DY, C, S, Bi, False, group, bits, lora_up=A, lora_down=us)
+        db = tq.lora_grad(DY, ts_t, 0)
+        da = tq.lora_grad(X, us_t, 1)
+        torch.cuda.synchronize()
+        out.update(dx=dx.float().cpu().numpy(), da=da.cpu().numpy(), db=db.cpu().numpy())
+    return out
+
+
+CASES = [
+    # (m, n, k, rank, alpha, bits, group, with_bias)
+    (512, 4864, 896, 8, 16.0, 4, 64, False),   # the single QLoRA linear workload
+    (48, 136, 192, 8, 16.0, 4, 64, True),
+    (200, 264, 384, 16, 32.0, 4, 32, False),
+    (130, 512, 256, 16, 32.0, 8, 128, True),
+    (64, 128, 128, 8, 8.0, 8, 64, False),
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", CASES, ids=lambda c: "m{}_n{}_k{}_r{}".format(*c[:4]))
+def test_adapted_linear_forward_and_backward(cuda, oracle, case):
+    import torobi_b200 as tq
+
+    m, n, k, r, alpha, bits, group, with_bias = case
+    rng = np.random.default_rng(1)
+    x = oracle.normal_bf16(rng, (m, k))
+    w = oracle.normal_bf16(rng, (n, k), 0.02)
+    a = oracle.normal_bf16(rng, (r, k), 1.0 / 8.0)
+    bl = oracle.normal_bf16(rng, (n, r), 0.01)
+    bias = oracle.normal_bf16(rng, (n,), 0.1) if with_bias else None
+    dy = oracle.normal_bf16(rng, (m, n))
+    c, s, b = oracle.quantize(w, bits, group)
+    scale = alpha / r
+    f = oracle.f32_from_bf16
+    y_ref, _ = oracle.qlora_linear_fwd(f(x), c, s, b, f(a), f(bl), scale, bits, group,
+                                       bias=f(bias) if bias is not None else None)
+    dx_ref, da_ref, db_ref = oracle.qlora_linear_bwd(f(x), f(dy), c, s, b, f(a), f(bl), scale,
+                                                     bits, group)
+    got = _run_adapted(tq, cuda, x, c, s, b, a, bl, scale, bits, group, bias, dy)
+    for name, ref in (("y", y_ref), ("dx", dx_ref), ("da", da_ref), ("db", db_ref)):
+        err = oracle.rel_err(got[name], ref)
+        assert err <= TOL, f"{name}: max rel err {err:.3e}"
+
+
+@pytest.mark.gpu
+def test_golden_qlora_fixture(cuda, oracle):
+    import torobi_b200 as tq
+
+    g = np.load(Path(__file__).parent / "golden" / "qlora.npz")
+    M, K, N, r, alpha, bits, group = (int(v) for v in g["meta"])
+    got = _run_adapted(tq, cuda, g["x"], g["codes"], g["scales"], g["biases"], g["lora_a"],
+                       g["lora_b"], alpha / r, bits, group, g["bias"], g["dy"])
+    f = oracle.f32_from_bf16
+    for name in ("y", "dx", "da", "db"):
+        err = oracle.rel_err(got[name], f(g[name]))
+        assert err <= TOL, f"{name}: max rel err {err:.3e}"
+
+
+@pytest.mark.gpu
+def test_zero_lora_b_gives_the_base_model_exactly(cuda, oracle):
+    """B starts at zero, so the adapted linear equals the base linear exactly
+    (the reference's test/lora_test.rb:140-148 asks the same of logits)."""
+    import torobi_b200 as tq
+
+    rng = np.random.default_rng(3)
+    m, n, k, r = 300, 384, 512, 16
+    x = oracle.normal_bf16(rng, (m, k))
+    w = oracle.normal_bf16(rng, (n, k), 0.02)
+    a = oracle.normal_bf16(rng, (r, k), 0.125)
+    bl = np.zeros((n, r), np.uint16)
+    c, s, b = oracle.quantize(w, 4, 64)
+    X = dev_bf16(x, cuda)
+    C, S, Bi = dev_u32(c, cuda), dev_bf16(s, cuda), dev_bf16(b, cuda)
+    base = tq.quantized_matmul(X, C, S, Bi, True, 64, 4)
+    ts, _ = tq.lora_down(X, dev_bf16(a, cuda), 2.0)
+    adapted = tq.qlora_matmul(X, C, S, Bi, True, 64, 4, lora_up=dev_bf16(bl, cuda), lora_down=ts)
+    assert np.array_equal(base.float().cpu().numpy(), adapted.float().cpu().numpy())
+
+
+@pytest.mark.gpu
+def test_lora_grad_accumulates_micro_batches(cuda, oracle):
+    """Gradients of two halves accumulated equal the gradient of the whole
+    (engine/src/state.rs:418-449: the gradient of a sum is the sum)."""
+    import torch
+    import torobi_b200 as tq
+
+    torch.manual_seed(5)
+    x = torch.randn(512, 640, device=cuda).bfloat16()
+    p_t = torch.randn(16, 512, device=cuda).bfloat16()
+    whole = tq.lora_grad(x, p_t.contiguous(), 1)
+    acc = torch.zeros(16, 640, device=cuda)
+    tq.lora_grad(x[:256], p_t[:, :256].contiguous(), 1, out=acc, accumulate=True)
+    tq.lora_grad(x[256:], p_t[:, 256:].contiguous(), 1, out=acc, accumulate=True)
+    # A ragged row count: the transposed operand carries a padded pitch.
+    ragged = tq.lora_grad(x[:203], torch.nn.functional.pad(p_t[:, :203], (0, 5)).contiguous(), 1)
+    assert torch.allclose(ragged, p_t[:, :203].float() @ x[:203].float(), rtol=1e-4, atol=1e-3)
+    ref = (p_t.float() @ x.float())
+    assert torch.allclose(whole, ref, rtol=1e-4, atol=1e-3)
+    assert torch.allclose(acc, ref, rtol=1e-4, atol=1e-3)

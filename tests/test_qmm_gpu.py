@@ -1,0 +1,105 @@
+"""Parity of quantized_matmul (forward and its VJP wrt x) with the oracle.
+
+Tolerance: max |got - want| / max |want| <= 1e-2 (bf16 operands, f32
+accumulation, bf16 output) -- the bar the quantized GEMMs are held to.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from _util import dev_bf16, dev_u32
+
+TOL = 1e-2
+
+# (m, w_rows, w_cols, bits, group): the single-linear workload first, then
+# ragged and tail shapes (m not a multiple of the token tile, w_rows not a
+# multiple of 128, w_cols with a half K-step at group 32).
+CASES = [
+    (512, 4864, 896, 4, 64),
+    (1, 128, 64, 4, 64),
+    (16, 1024, 512, 4, 64),
+    (17, 136, 96, 4, 32),
+    (100, 200, 256, 8, 128),
+    (300, 264, 384, 8, 32),
+    (257, 128, 128, 4, 128),
+    (129, 392, 640, 4, 32),
+    (640, 256, 1024, 8, 64),
+]
+
+
+def _setup(oracle, seed, m, n, k, bits, group):
+    rng = np.random.default_rng(seed)
+    x = oracle.normal_bf16(rng, (m, k))
+    w = oracle.normal_bf16(rng, (n, k), 0.02)
+    dy = oracle.normal_bf16(rng, (m, n))
+    c, s, b = oracle.quantize(w, bits, group)
+    return x, dy, c, s, b
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", CASES, ids=lambda c: "m{}_n{}_k{}_b{}_g{}".format(*c))
+def test_quantized_matmul_forward(cuda, oracle, case):
+    import torobi_b200 as tq
+
+    m, n, k, bits, group = case
+    x, _, c, s, b = _setup(oracle, 11, m, n, k, bits, group)
+    want = oracle.qmm_fwd(x, c, s, b, bits, group)
+    y = tq.quantized_matmul(dev_bf16(x, cuda), dev_u32(c, cuda), dev_bf16(s, cuda),
+                            dev_bf16(b, cuda), transpose=True, group_size=group, bits=bits)
+    got = y.float().cpu().numpy()
+    err = oracle.rel_err(got, want)
+    assert err <= TOL, f"max rel err {err:.3e}"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", CASES, ids=lambda c: "m{}_n{}_k{}_b{}_g{}".format(*c))
+def test_quantized_matmul_backward_dx(cuda, oracle, case):
+    import torobi_b200 as tq
+
+    m, n, k, bits, group = case
+    _, dy, c, s, b = _setup(oracle, 12, m, n, k, bits, group)
+    want = oracle.qmm_dx(dy, c, s, b, bits, group)
+    dx = tq.quantized_matmul(dev_bf16(dy, cuda), dev_u32(c, cuda), dev_bf16(s, cuda),
+                             dev_bf16(b, cuda), transpose=False, group_size=group, bits=bits)
+    got = dx.float().cpu().numpy()
+    err = oracle.rel_err(got, want)
+    assert err <= TOL, f"max rel err {err:.3e}"
+
+
+@pytest.mark.gpu
+def test_quantized_matmul_matches_dequantized_weight(cuda):
+    """quantized_matmul(x, W) equals x . dequantize(W)^T computed in f32 by torch
+    on the same dequantized bf16 weight (the dequant inside the GEMM is the
+    dequantize kernel's, bit for bit, so only accumulation order differs)."""
+    import torch
+    import torobi_b200 as tq
+
+    torch.manual_seed(0)
+    w = (torch.randn(1024, 2048, device=cuda) * 0.02).bfloat16()
+    x = torch.randn(384, 2048, device=cuda).bfloat16()
+    c, s, b = tq.quantize(w, 64, 4)
+    wd = tq.dequantize(c, s, b, 64, 4).float()
+    ref = x.float() @ wd.t()
+    y = tq.quantized_matmul(x, c, s, b, True, 64, 4).float()
+    assert ((y - ref).abs().max() / ref.abs().max()).item() < 4e-3
+    dy = torch.randn(384, 1024, device=cuda).bfloat16()
+    ref_dx = dy.float() @ wd
+    dx = tq.quantized_matmul(dy, c, s, b, False, 64, 4).float()
+    assert ((dx - ref_dx).abs().max() / ref_dx.abs().max()).item() < 4e-3
+
+
+@pytest.mark.gpu
+def test_quantized_matmul_argument_errors(cuda):
+    import torch
+    import torobi_b200 as tq
+
+    w = torch.zeros((128, 256), dtype=torch.bfloat16, device=cuda)
+    c, s, b = tq.quantize(w, 64, 4)
+    x = torch.zeros((4, 255), dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(ValueError, match="last dimension"):
+        tq.quantized_matmul(x, c, s, b)
+    with pytest.raises(ValueError, match="scales"):
+        tq.quantized_matmul(torch.zeros((4, 256), dtype=torch.bfloat16, device=cuda), c, s[:, :2], b)
+    y = tq.quantized_matmul(torch.zeros((0, 256), dtype=torch.bfloat16, device=cuda), c, s, b)
+    assert y.shape == (0, 128)

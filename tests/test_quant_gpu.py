@@ -1,0 +1,126 @@
+"""Parity of the quantize / dequantize kernels with the oracle: bit-exact.
+
+Shapes are every linear of a Qwen2.5-0.5B-shaped layer (hidden 896,
+intermediate 4864, 14/2 heads of dim 64), weights N(0, 0.02) plus 0.1%
+outliers at +-0.5, bits {4, 8} x group {32, 64, 128}: the quantize sweep
+the benchmark runs, on seeded synthetic weights.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from _util import bf16_equal, dev_bf16, first_mismatch, host_bf16, host_u32
+
+QWEN_SHAPES = {
+    "q_proj/o_proj": (896, 896),
+    "k_proj/v_proj": (128, 896),
+    "gate_proj/up_proj": (4864, 896),
+    "down_proj": (896, 4864),
+}
+
+
+def _check_quantize(tq, oracle, w, bits, group, device):
+    codes, scales, biases = oracle.quantize(w, bits, group)
+    tc, ts, tb = tq.quantize(dev_bf16(w, device), group, bits)
+    got_c = host_u32(tc)
+    assert np.array_equal(got_c, codes), first_mismatch(got_c, codes)
+    assert bf16_equal(host_bf16(ts), scales), first_mismatch(host_bf16(ts), scales)
+    assert bf16_equal(host_bf16(tb), biases), first_mismatch(host_bf16(tb), biases)
+    deq = tq.dequantize(tc, ts, tb, group, bits)
+    want = oracle.dequantize(codes, scales, biases, bits, group)
+    assert bf16_equal(host_bf16(deq), want), first_mismatch(host_bf16(deq), want)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("group", [32, 64, 128])
+def test_quantize_bit_exact_on_qwen_shapes(cuda, oracle, bits, group):
+    import torobi_b200 as tq
+
+    rng = np.random.default_rng(1000 + bits * 10 + group)
+    for shape in QWEN_SHAPES.values():
+        w = oracle.weights_with_outliers(rng, shape)
+        _check_quantize(tq, oracle, w, bits, group, cuda)
+
+
+def _edge_matrix(oracle, cols):
+    f = np.float32
+    rows = []
+    rows.append(np.zeros(cols, f))                                  # all zero
+    rows.append(np.full(cols, 0.75, f))                             # constant positive
+    rows.append(np.full(cols, -3.0, f))                             # constant negative
+    rows.append(-np.abs(np.linspace(0.1, 2.0, cols, dtype=f)))      # all negative
+    rows.append(np.abs(np.linspace(0.1, 2.0, cols, dtype=f)))       # all positive
+    rows.append(np.linspace(-1.0, 0.5, cols, dtype=f))              # |min| > |max|
+    rows.append(np.linspace(-0.5, 1.0, cols, dtype=f))              # |max| > |min|
+    rows.append(np.full(cols, 1e-40, f))                            # subnormal (bf16 denormal)
+    r = np.linspace(-1e38, 3e38, cols, dtype=f); rows.append(r)     # near the top of the range
+    r = np.linspace(-1.0, 1.0, cols, dtype=f); r[3] = np.nan; rows.append(r)   # a NaN element
+    r = np.linspace(-1.0, 1.0, cols, dtype=f); r[5] = np.inf; rows.append(r)   # +inf
+    r = np.linspace(-1.0, 1.0, cols, dtype=f); r[7] = -np.inf; rows.append(r)  # -inf
+    r = np.zeros(cols, f); r[::2] = -0.0; r[1] = 1e-3; rows.append(r)          # signed zeros
+    r = np.linspace(1.0, 1.0001, cols, dtype=f); rows.append(r)     # nearly constant: huge q0
+    return oracle.bf16_from_f32(np.stack(rows))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("group", [32, 64, 128])
+def test_quantize_edge_values_bit_exact(cuda, oracle, bits, group):
+    import torobi_b200 as tq
+
+    _check_quantize(tq, oracle, _edge_matrix(oracle, 256), bits, group, cuda)
+
+
+@pytest.mark.gpu
+def test_quantize_ragged_and_tiny_shapes(cuda, oracle):
+    import torobi_b200 as tq
+
+    rng = np.random.default_rng(7)
+    for rows, cols in [(1, 32), (3, 64), (5, 96), (7, 128), (33, 160), (1, 4864)]:
+        for bits, group in [(4, 32), (8, 32), (4, 64)]:
+            if cols % group:
+                continue
+            w = oracle.normal_bf16(rng, (rows, cols), 0.02)
+            _check_quantize(tq, oracle, w, bits, group, cuda)
+
+
+@pytest.mark.gpu
+def test_golden_quantize_fixture(cuda, oracle):
+    import torobi_b200 as tq
+    from pathlib import Path
+
+    g = np.load(Path(__file__).parent / "golden" / "quantize.npz")
+    for key in sorted(k for k in g.files if k.startswith("w_")):
+        tag = key[2:]
+        bits, group = (int(v) for v in tag.split("_"))
+        tc, ts, tb = tq.quantize(dev_bf16(g[key], cuda), group, bits)
+        assert np.array_equal(host_u32(tc), g[f"codes_{tag}"])
+        assert bf16_equal(host_bf16(ts), g[f"scales_{tag}"])
+        assert bf16_equal(host_bf16(tb), g[f"biases_{tag}"])
+        deq = tq.dequantize(tc, ts, tb, group, bits)
+        assert bf16_equal(host_bf16(deq), g[f"deq_{tag}"])
+
+
+@pytest.mark.gpu
+def test_quantize_errors_and_empty(cuda):
+    import torch
+    import torobi_b200 as tq
+
+    w = torch.zeros((4, 96), dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(ValueError, match="divisible"):
+        tq.quantize(w, 64, 4)
+    with pytest.raises(ValueError, match="bits"):
+        tq.quantize(w, 32, 3)
+    with pytest.raises(ValueError, match="group size"):
+        tq.quantize(w, 16, 4)
+    with pytest.raises(ValueError, match="bfloat16"):
+        tq.quantize(w.float(), 32, 4)
+    with pytest.raises(ValueError, match="CUDA"):
+        tq.quantize(w.cpu(), 32, 4)
+    empty = torch.zeros((0, 64), dtype=torch.bfloat16, device=cuda)
+    c, s, b = tq.quantize(empty, 64, 4)
+    assert c.shape == (0, 8) and s.shape == (0, 1) and b.shape == (0, 1)
+    d = tq.dequantize(c, s, b, 64, 4)
+    assert d.shape == (0, 64)

@@ -1,0 +1,527 @@
+// quantized_matmul on the 5th-generation tensor cores (tcgen05 / TMEM), with
+// the LoRA up-projection and the linear's bias fused into the accumulator.
+//
+// One CTA computes a 128 x BN tile of the output TRANSPOSED in tensor memory:
+// the UMMA's M side (128 TMEM lanes) is the weight's output features and its
+// N side (BN columns) is the tokens.  Putting the quantized weight on the M
+// side halves the dequantization work per MMA flop against the other
+// orientation (a 128-row weight tile feeds a 128 x BN MMA instead of a BN-row
+// tile feeding a BN x 128 one).
+//
+//   warp 0      TMA producer: activation tile (bf16, 128B swizzle) and the raw
+//               packed-code tile of each stage; the LoRA tiles once.
+//   warp 1      TMEM allocator and the single UMMA-issuing thread.
+//   warps 2-5   dequantizers: packed codes (shared) -> bf16 weight tile in the
+//               UMMA canonical 128B-swizzled layout, w = RNE(scale*q + bias);
+//               afterwards the epilogue (TMEM -> registers -> bf16 -> global).
+//
+// transpose (linear forward, y = x . W^T): the reduction runs along W's packed
+// axis, so the dequantized tile is K-major.  Backward wrt x (y = dy . W): the
+// reduction runs along W's rows and the output along its packed axis, so the
+// same tile is written MN-major -- the same kernel with the roles swapped.
+//
+// The LoRA branch: lora_down (the [m, rank] scaled down-projection) and
+// lora_up (B [n, rank] forward, A [rank, k] backward) are loaded once and one
+// extra K=16 UMMA adds lora_up . lora_down^T into the same accumulator before
+// the main loop, so base + adapter leave TMEM with one rounding to bf16.
+#include <cuda_bf16.h>
+
+#include "tq_ptx.cuh"
+#include "tq_runtime.h"
+
+namespace tq {
+namespace {
+
+constexpr int kBM = 128;        // weight-side rows per CTA (UMMA M)
+constexpr int kBK = 64;         // reduction elements per pipeline stage
+constexpr int kThreads = 192;   // 6 warps
+constexpr int kSmemLimit = 232448;
+
+template <int BITS, bool TRANS, int BN>
+struct Cfg {
+  static constexpr int X_BYTES = BN * kBK * 2;
+  static constexpr int A_BYTES = kBM * kBK * 2;
+  static constexpr int C_BYTES = kBM * kBK * BITS / 8;
+  static constexpr int STAGE_BYTES = X_BYTES + A_BYTES + C_BYTES;
+  static constexpr int LUP_BYTES = kBM * 16 * 2;            // [128 x 16] bf16
+  static constexpr int LDN_BYTES = BN * 16 * 2;             // [BN x 16] bf16
+  static constexpr int LORA_BYTES = ((LUP_BYTES + LDN_BYTES + 1023) / 1024) * 1024;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int STAGES_RAW = (kSmemLimit - 1024 - LORA_BYTES - BAR_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 6 ? 6 : STAGES_RAW;
+  static constexpr int SMEM = 1024 + LORA_BYTES + STAGES * STAGE_BYTES + BAR_BYTES;
+  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+  static_assert(STAGES >= 2, "shared memory too small for two stages");
+  static_assert(SMEM <= kSmemLimit, "shared memory budget");
+};
+
+struct Params {
+  const uint16_t* scales;
+  const uint16_t* biases;
+  const uint16_t* bias_vec;  // [n_out] bf16 or null
+  uint16_t* y;               // [m, n_out] bf16
+  int m;
+  int n_out;                 // output features of this GEMM
+  int k_red;                 // reduction length
+  int w_rows;                // rows of the stored weight
+  int groups_per_row;        // w_cols / group_size
+  int group_shift;
+  int lora_rank;             // 0, 8 or 16
+  int* status;
+};
+
+__device__ __forceinline__ uint16_t ldg_u16(const uint16_t* p) {
+  return __ldg(reinterpret_cast<const unsigned short*>(p));
+}
+
+template <int BITS, bool TRANS, int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    qmm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_c,
+               const __grid_constant__ CUtensorMap tm_lup,
+               const __grid_constant__ CUtensorMap tm_ldn, const Params p) {
+  using C = Cfg<BITS, TRANS, BN>;
+  constexpr int S = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* const gbase = smem_raw + (base - raw);
+
+  const uint32_t lup = base;                                  // LoRA up tile
+  const uint32_t ldn = base + C::LUP_BYTES;                   // LoRA down tile
+  const uint32_t stages = base + C::LORA_BYTES;
+  auto x_s = [&](int s) { return stages + s * C::STAGE_BYTES; };
+  auto a_s = [&](int s) { return stages + s * C::STAGE_BYTES + C::X_BYTES; };
+  auto c_s = [&](int s) { return stages + s * C::STAGE_BYTES + C::X_BYTES + C::A_BYTES; };
+  const uint32_t bars = stages + S * C::STAGE_BYTES;
+  auto full_b = [&](int s) { return bars + 8u * s; };
+  auto wready_b = [&](int s) { return bars + 8u * (S + s); };
+  auto empty_b = [&](int s) { return bars + 8u * (2 * S + s); };
+  const uint32_t lora_b = bars + 8u * (3 * S);
+  const uint32_t acc_b = bars + 8u * (3 * S + 1);
+  const uint32_t tmem_slot = bars + 8u * (3 * S + 2);
+  volatile uint32_t* tmem_slot_ptr =
+      reinterpret_cast<volatile uint32_t*>(gbase + (tmem_slot - base));
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int out0 = blockIdx.x * kBM;
+  const int m0 = blockIdx.y * BN;
+  const int num_k = (p.k_red + kBK - 1) / kBK;
+  const bool has_lora = p.lora_rank > 0;
+  const int lora_chunks = p.lora_rank / 8;
+
+  // Zero the LoRA tiles: with rank 8 the second K-chunk stays zero.
+  if (has_lora) {
+    for (int i = threadIdx.x; i < C::LORA_BYTES / 16; i += kThreads)
+      sts128(base + 16u * i, 0u, 0u, 0u, 0u);
+    fence_proxy_async_smem();
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full_b(s), 1);
+      mbar_init(wready_b(s), 4);
+      mbar_init(empty_b(s), 1);
+    }
+    mbar_init(lora_b, 1);
+    mbar_init(acc_b, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot_ptr;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one_sync()) {
+      tma_prefetch_desc(&tm_x);
+      tma_prefetch_desc(&tm_c);
+      if (has_lora) {
+        tma_prefetch_desc(&tm_lup);
+        tma_prefetch_desc(&tm_ldn);
+        const uint32_t bytes = lora_chunks * (kBM * 16 + BN * 16);
+        mbar_arrive_expect_tx(lora_b, bytes);
+        for (int ch = 0; ch < lora_chunks; ++ch) {
+          if constexpr (TRANS) {
+            // B [n_out, rank]: K-major, no swizzle; chunk = 8 rank columns.
+            tma_load_2d(lup + ch * kBM * 16, &tm_lup, lora_b, ch * 8, out0);
+          } else {
+            // A [rank, k]: MN-major 128B-swizzled atoms (64 k x 8 rank).
+            tma_load_2d(lup + ch * 1024, &tm_lup, lora_b, out0, ch * 8);
+            tma_load_2d(lup + 2048 + ch * 1024, &tm_lup, lora_b, out0 + 64, ch * 8);
+          }
+          tma_load_2d(ldn + ch * BN * 16, &tm_ldn, lora_b, ch * 8, m0);
+        }
+      }
+      bool ok = true;
+      int issued = 0;
+      for (int i = 0; i < num_k && ok; ++i) {
+        const int s = i % S;
+        const uint32_t ph = (i / S) & 1;
+        ok = mbar_wait(empty_b(s), ph ^ 1, p.status);
+        if (!ok) break;
+        mbar_arrive_expect_tx(full_b(s), C::X_BYTES + C::C_BYTES);
+        tma_load_2d(x_s(s), &tm_x, full_b(s), i * kBK, m0);
+        if constexpr (TRANS)
+          tma_load_2d(c_s(s), &tm_c, full_b(s), i * kBK * BITS / 32, out0);
+        else
+          tma_load_2d(c_s(s), &tm_c, full_b(s), out0 * BITS / 32, i * kBK);
+        ++issued;
+      }
+      // Never leave a copy in flight: wait for the last phase of every stage.
+      for (int i = issued - S < 0 ? 0 : issued - S; i < issued; ++i)
+        mbar_wait(full_b(i % S), (i / S) & 1, p.status);
+      if (has_lora) mbar_wait(lora_b, 0, p.status);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (elect_one_sync()) {
+      constexpr uint32_t idesc = make_idesc_bf16(kBM, BN, !TRANS, false);
+      uint32_t acc = 0;
+      bool ok = true;
+      if (has_lora) {
+        ok = mbar_wait(lora_b, 0, p.status);
+        tc_fence_after();
+        uint64_t adesc;
+        if constexpr (TRANS)
+          adesc = make_sdesc(lup, kBM * 16, 128, kSwNone);  // LBO: K chunk, SBO: 8-row group
+        else
+          adesc = make_sdesc(lup, 2048, 1024, kSw128);     // LBO: MN atom, SBO: K group
+        const uint64_t bdesc = make_sdesc(ldn, BN * 16, 128, kSwNone);
+        if (ok) {
+          umma_bf16(tmem, adesc, bdesc, idesc, 0);
+          acc = 1;
+        }
+      }
+      for (int i = 0; i < num_k && ok; ++i) {
+        const int s = i % S;
+        const uint32_t ph = (i / S) & 1;
+        ok = mbar_wait(full_b(s), ph, p.status) && mbar_wait(wready_b(s), ph, p.status);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          uint64_t adesc;
+          if constexpr (TRANS)
+            adesc = make_sdesc(a_s(s) + kk * 32, 16, 1024, kSw128);
+          else
+            adesc = make_sdesc(a_s(s) + kk * 2048, 8192, 1024, kSw128);
+          const uint64_t bdesc = make_sdesc(x_s(s) + kk * 32, 16, 1024, kSw128);
+          umma_bf16(tmem, adesc, bdesc, idesc, acc);
+          acc = 1;
+        }
+        umma_commit(empty_b(s));
+      }
+      umma_commit(acc_b);
+      mbar_wait(acc_b, 0, p.status);  // nothing may outlive the CTA's TMEM
+    }
+  } else {
+    // ---------------------------------------------------- dequant warps
+    const int t = threadIdx.x - 64;  // 0..127
+    const uint32_t gpr = static_cast<uint32_t>(p.groups_per_row);
+    bool ok = true;
+    for (int i = 0; i < num_k && ok; ++i) {
+      const int s = i % S;
+      const uint32_t ph = (i / S) & 1;
+      const int k0 = i * kBK;
+      // Scale/bias for this thread's elements (two groups at most).
+      uint32_t s2[2], b2[2];
+      if constexpr (TRANS) {
+        const int row = out0 + t;  // weight row
+        const uint32_t g0 = static_cast<uint32_t>(k0) >> p.group_shift;
+        const uint32_t g1 = static_cast<uint32_t>(k0 + 32) >> p.group_shift;
+        const bool rv = row < p.n_out;
+        const size_t rb = static_cast<size_t>(row) * gpr;
+        s2[0] = (rv && g0 < gpr) ? bf16_dup(ldg_u16(p.scales + rb + g0)) : 0u;
+        b2[0] = (rv && g0 < gpr) ? bf16_dup(ldg_u16(p.biases + rb + g0)) : 0u;
+        s2[1] = (rv && g1 < gpr) ? bf16_dup(ldg_u16(p.scales + rb + g1)) : 0u;
+        b2[1] = (rv && g1 < gpr) ? bf16_dup(ldg_u16(p.biases + rb + g1)) : 0u;
+      } else {
+        const int kr = t & 63;
+        const int h = t >> 6;
+        const int row = k0 + kr;  // weight row (reduction index)
+        const uint32_t g0 = static_cast<uint32_t>(out0 + 64 * h) >> p.group_shift;
+        const uint32_t g1 = static_cast<uint32_t>(out0 + 64 * h + 32) >> p.group_shift;
+        const bool rv = row < p.w_rows;
+        const size_t rb = static_cast<size_t>(row) * gpr;
+        s2[0] = (rv && g0 < gpr) ? bf16_dup(ldg_u16(p.scales + rb + g0)) : 0u;
+        b2[0] = (rv && g0 < gpr) ? bf16_dup(ldg_u16(p.biases + rb + g0)) : 0u;
+        s2[1] = (rv && g1 < gpr) ? bf16_dup(ldg_u16(p.scales + rb + g1)) : 0u;
+        b2[1] = (rv && g1 < gpr) ? bf16_dup(ldg_u16(p.biases + rb + g1)) : 0u;
+      }
+      ok = mbar_wait(full_b(s), ph, p.status);
+      if (!ok) break;
+      const uint32_t cb = c_s(s);
+      const uint32_t ab = a_s(s);
+      if constexpr (TRANS) {
+        const int r = t;
+        if constexpr (BITS == 4) {
+          uint32_t w[8];
+          lds128(cb + swz<32>(r * 32), w[0], w[1], w[2], w[3]);
+          lds128(cb + swz<32>(r * 32 + 16), w[4], w[5], w[6], w[7]);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint32_t o[4];
+            dequant_u4x8(w[j], s2[j >> 2], b2[j >> 2], o);
+            sts128(ab + r * 128 + ((j ^ (r & 7)) << 4), o[0], o[1], o[2], o[3]);
+          }
+        } else {
+          uint32_t w[16];
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            lds128(cb + swz<64>(r * 64 + c * 16), w[4 * c], w[4 * c + 1], w[4 * c + 2],
+                   w[4 * c + 3]);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint32_t o0[2], o1[2];
+            dequant_u8x4(w[2 * j], s2[j >> 2], b2[j >> 2], o0);
+            dequant_u8x4(w[2 * j + 1], s2[j >> 2], b2[j >> 2], o1);
+            sts128(ab + r * 128 + ((j ^ (r & 7)) << 4), o0[0], o0[1], o1[0], o1[1]);
+          }
+        }
+      } else {
+        const int kr = t & 63;
+        const int h = t >> 6;
+        const uint32_t row_off = h * 8192 + (kr >> 3) * 1024 + (kr & 7) * 128;
+        if constexpr (BITS == 4) {
+          uint32_t w[8];
+          lds128(cb + swz<64>(kr * 64 + (2 * h) * 16), w[0], w[1], w[2], w[3]);
+          lds128(cb + swz<64>(kr * 64 + (2 * h + 1) * 16), w[4], w[5], w[6], w[7]);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint32_t o[4];
+            dequant_u4x8(w[j], s2[j >> 2], b2[j >> 2], o);
+            sts128(ab + row_off + ((j ^ (kr & 7)) << 4), o[0], o[1], o[2], o[3]);
+          }
+        } else {
+          uint32_t w[16];
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            lds128(cb + swz<128>(kr * 128 + (4 * h + c) * 16), w[4 * c], w[4 * c + 1],
+                   w[4 * c + 2], w[4 * c + 3]);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint32_t o0[2], o1[2];
+            dequant_u8x4(w[2 * j], s2[j >> 2], b2[j >> 2], o0);
+            dequant_u8x4(w[2 * j + 1], s2[j >> 2], b2[j >> 2], o1);
+            sts128(ab + row_off + ((j ^ (kr & 7)) << 4), o0[0], o0[1], o1[0], o1[1]);
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(wready_b(s));
+    }
+
+    // ------------------------------------------------------------ epilogue
+    ok = mbar_wait(acc_b, 0, p.status) && ok;
+    tc_fence_after();
+    const int q = warp & 3;              // TMEM lane quadrant this warp may read
+    const int r = q * 32 + lane;         // output feature within the tile
+    const int og = out0 + r;
+    float bias = 0.0f;
+    if (p.bias_vec && og < p.n_out) bias = __uint_as_float(uint32_t(ldg_u16(p.bias_vec + og)) << 16);
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, v);
+      tmem_ld_wait();
+      if (og < p.n_out) {
+        const int mlim = p.m - (m0 + c0);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (j < mlim) {
+            const float f = __uint_as_float(v[j]) + bias;
+            p.y[static_cast<size_t>(m0 + c0 + j) * p.n_out + og] =
+                __bfloat16_as_ushort(__float2bfloat16_rn(f));
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+struct Args {
+  const void* x;
+  const void* codes;
+  const void* scales;
+  const void* biases;
+  const void* bias;
+  const void* lora_up;
+  const void* lora_down;
+  int64_t m, w_rows, w_cols;
+  int transpose, group_size, bits;
+  int rank;
+  void* y;
+};
+
+template <int BITS, bool TRANS, int BN>
+int launch(const Args& a, cudaStream_t stream, int* status) {
+  using C = Cfg<BITS, TRANS, BN>;
+  const int64_t k_red = TRANS ? a.w_cols : a.w_rows;
+  const int64_t n_out = TRANS ? a.w_rows : a.w_cols;
+  CUtensorMap tm_x, tm_c, tm_lup, tm_ldn;
+  int rc;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(k_red), static_cast<uint64_t>(a.m)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(k_red) * 2};
+    const uint32_t box[2] = {kBK, BN};
+    rc = encode_tmap(&tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.x, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t words = static_cast<uint64_t>(a.w_cols) * BITS / 32;
+    const uint64_t dims[2] = {words, static_cast<uint64_t>(a.w_rows)};
+    const uint64_t strides[1] = {words * 4};
+    uint32_t box[2];
+    CUtensorMapSwizzle sw;
+    if constexpr (TRANS) {
+      box[0] = kBK * BITS / 32;
+      box[1] = kBM;
+      sw = BITS == 4 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B;
+    } else {
+      box[0] = kBM * BITS / 32;
+      box[1] = kBK;
+      sw = BITS == 4 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+    }
+    rc = encode_tmap(&tm_c, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, a.codes, dims, strides, box, sw);
+    if (rc) return rc;
+  }
+  if (a.rank > 0) {
+    if constexpr (TRANS) {
+      const uint64_t dims[2] = {static_cast<uint64_t>(a.rank), static_cast<uint64_t>(a.w_rows)};
+      const uint64_t strides[1] = {static_cast<uint64_t>(a.rank) * 2};
+      const uint32_t box[2] = {8, kBM};
+      rc = encode_tmap(&tm_lup, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.lora_up, dims, strides, box,
+                       CU_TENSOR_MAP_SWIZZLE_NONE);
+    } else {
+      const uint64_t dims[2] = {static_cast<uint64_t>(a.w_cols), static_cast<uint64_t>(a.rank)};
+      const uint64_t strides[1] = {static_cast<uint64_t>(a.w_cols) * 2};
+      const uint32_t box[2] = {64, 8};
+      rc = encode_tmap(&tm_lup, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.lora_up, dims, strides, box,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+    if (rc) return rc;
+    const uint64_t dims[2] = {static_cast<uint64_t>(a.rank), static_cast<uint64_t>(a.m)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(a.rank) * 2};
+    const uint32_t box[2] = {8, BN};
+    rc = encode_tmap(&tm_ldn, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.lora_down, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  } else {
+    tm_lup = tm_x;
+    tm_ldn = tm_x;
+  }
+  Params p;
+  p.scales = static_cast<const uint16_t*>(a.scales);
+  p.biases = static_cast<const uint16_t*>(a.biases);
+  p.bias_vec = static_cast<const uint16_t*>(a.bias);
+  p.y = static_cast<uint16_t*>(a.y);
+  p.m = static_cast<int>(a.m);
+  p.n_out = static_cast<int>(n_out);
+  p.k_red = static_cast<int>(k_red);
+  p.w_rows = static_cast<int>(a.w_rows);
+  p.groups_per_row = static_cast<int>(a.w_cols / a.group_size);
+  p.group_shift = a.group_size == 32 ? 5 : (a.group_size == 64 ? 6 : 7);
+  p.lora_rank = a.rank;
+  p.status = status;
+  auto kernel = qmm_kernel<BITS, TRANS, BN>;
+  rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
+                  "cudaFuncSetAttribute(qmm smem)");
+  if (rc) return rc;
+  const dim3 grid(static_cast<unsigned>((n_out + kBM - 1) / kBM),
+                  static_cast<unsigned>((a.m + BN - 1) / BN));
+  kernel<<<grid, kThreads, C::SMEM, stream>>>(tm_x, tm_c, tm_lup, tm_ldn, p);
+  return check_cuda(cudaGetLastError(), "qmm launch");
+}
+
+template <int BITS, bool TRANS>
+int launch_bn(const Args& a, cudaStream_t stream, int* status) {
+  const int64_t n_out = TRANS ? a.w_rows : a.w_cols;
+  const int64_t tiles_n = (n_out + kBM - 1) / kBM;
+  const int sms = sm_count();
+  // Largest token tile that still gives every SM a CTA (M-side padding is
+  // zero-filled by TMA and never stored).
+  int bn = 32;
+  for (int cand : {256, 128, 64}) {
+    if (a.m >= cand / 2 && ((a.m + cand - 1) / cand) * tiles_n >= sms) {
+      bn = cand;
+      break;
+    }
+  }
+  if (bn == 32 && a.m > 32) bn = a.m > 128 ? 128 : 64;
+  switch (bn) {
+    case 256: return launch<BITS, TRANS, 256>(a, stream, status);
+    case 128: return launch<BITS, TRANS, 128>(a, stream, status);
+    case 64: return launch<BITS, TRANS, 64>(a, stream, status);
+    default: return launch<BITS, TRANS, 32>(a, stream, status);
+  }
+}
+
+int run(const Args& a, void* stream) {
+  if (a.bits != 4 && a.bits != 8) return fail(TQ_ERR_UNSUPPORTED, "bits must be 4 or 8, got %d", a.bits);
+  if (a.group_size != 32 && a.group_size != 64 && a.group_size != 128)
+    return fail(TQ_ERR_UNSUPPORTED, "group_size must be 32, 64 or 128, got %d", a.group_size);
+  if (a.m < 0 || a.w_rows < 0 || a.w_cols < 0) return fail(TQ_ERR_INVALID, "negative shape");
+  if (a.w_cols % a.group_size != 0)
+    return fail(TQ_ERR_INVALID, "w_cols (%lld) must be divisible by group_size (%d)",
+                (long long)a.w_cols, a.group_size);
+  if (a.w_rows % 8 != 0)
+    return fail(TQ_ERR_INVALID, "w_rows (%lld) must be a multiple of 8", (long long)a.w_rows);
+  if (a.m > (1ll << 31) - 1 || a.w_rows > (1ll << 31) - 1 || a.w_cols > (1ll << 31) - 1)
+    return fail(TQ_ERR_INVALID, "dimensions must fit in 31 bits");
+  if (a.rank != 0 && a.rank != 8 && a.rank != 16)
+    return fail(TQ_ERR_UNSUPPORTED, "LoRA rank must be 8 or 16 (or 0 for none), got %d", a.rank);
+  if (a.rank && (!a.lora_up || !a.lora_down))
+    return fail(TQ_ERR_INVALID, "rank %d needs both lora_up and lora_down", a.rank);
+  if (!a.transpose && a.bias) return fail(TQ_ERR_INVALID, "bias is only defined for transpose != 0");
+  if (a.m == 0 || a.w_rows == 0 || a.w_cols == 0) return TQ_OK;
+  if (!a.x || !a.codes || !a.scales || !a.biases || !a.y) return fail(TQ_ERR_INVALID, "null pointer");
+  if (!aligned(a.x, 16) || !aligned(a.codes, 16) || (a.rank && (!aligned(a.lora_up, 16) ||
+                                                                 !aligned(a.lora_down, 16))))
+    return fail(TQ_ERR_MISALIGNED, "x, codes, lora_up and lora_down must be 16-byte aligned");
+  if (!aligned(a.y, 2) || !aligned(a.scales, 2) || !aligned(a.biases, 2))
+    return fail(TQ_ERR_MISALIGNED, "y, scales and biases must be 2-byte aligned");
+  int rc = TQ_OK;
+  int* status = device_status_ptr(&rc);
+  if (!status) return rc;
+  cudaStream_t s = as_stream(stream);
+  if (a.bits == 4)
+    return a.transpose ? launch_bn<4, true>(a, s, status) : launch_bn<4, false>(a, s, status);
+  return a.transpose ? launch_bn<8, true>(a, s, status) : launch_bn<8, false>(a, s, status);
+}
+
+}  // namespace
+}  // namespace tq
+
+extern "C" int tq_quantized_matmul(const void* x, const void* codes, const void* scales,
+                                   const void* biases, int64_t m, int64_t w_rows, int64_t w_cols,
+                                   int transpose, int group_size, int bits, void* y, void* stream) {
+  tq::Args a{x, codes, scales, biases, nullptr, nullptr, nullptr, m, w_rows, w_cols,
+             transpose, group_size, bits, 0, y};
+  return tq::run(a, stream);
+}
+
+extern "C" int tq_qlora_matmul(const void* x, const void* codes, const void* scales,
+                               const void* biases, int64_t m, int64_t w_rows, int64_t w_cols,
+                               int transpose, int group_size, int bits, const void* bias,
+                               const void* lora_up, const void* lora_down, int64_t rank, void* y,
+                               void* stream) {
+  if (rank < 0 || rank > 16) return tq::fail(TQ_ERR_UNSUPPORTED, "LoRA rank must be 8 or 16");
+  tq::Args a{x, codes, scales, biases, bias, lora_up, lora_down, m, w_rows, w_cols,
+             transpose, group_size, bits, static_cast<int>(rank), y};
+  return tq::run(a, stream);
+}

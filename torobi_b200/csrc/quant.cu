@@ -1,0 +1,219 @@
+// Affine quantize / dequantize kernels (MLX layout) and their C entry points.
+//
+// Both are HBM-bound streams: quantize reads 2 bytes per element and writes
+// bits/8 + 4/group_size; dequantize the reverse.  Each thread owns whole
+// 16-byte vectors so every global access is a 128-bit transaction, and a
+// group's min/max is reduced across the group_size/8 lanes that hold it with
+// warp shuffles (groups never straddle a warp: 32 lanes x 8 elements covers a
+// whole number of groups for group_size in {32, 64, 128}).
+#include <cuda_bf16.h>
+
+#include "tq_ptx.cuh"
+#include "tq_runtime.h"
+
+namespace tq {
+namespace {
+
+__device__ __forceinline__ float mlx_max(float a, float b) { return a < b ? b : a; }
+__device__ __forceinline__ float mlx_min(float a, float b) { return b < a ? b : a; }
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint32_t h) { return __uint_as_float(h << 16); }
+
+// f32 -> bf16 bits, round to nearest even (NaN -> canonical quiet NaN 0x7FC0).
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
+  if (f != f) return 0x7FC0;
+  const uint32_t u = __float_as_uint(f);
+  return static_cast<uint16_t>((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+}
+
+// One thread = 8 consecutive elements (one 16-byte vector).  LANES = lanes per
+// group = group_size / 8.
+template <int BITS, int LANES>
+__global__ void __launch_bounds__(256) quantize_kernel(const uint4* __restrict__ w,
+                                                       int64_t n_vec, uint32_t* __restrict__ codes,
+                                                       uint16_t* __restrict__ scales,
+                                                       uint16_t* __restrict__ biases) {
+  constexpr float n_bins = static_cast<float>((1 << BITS) - 1);
+  constexpr float eps = 1e-7f;
+  const int lane = threadIdx.x & 31;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  // Iterate whole warps so shuffles always see 32 lanes.
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31);
+       base < n_vec; base += stride) {
+    const int64_t vi = base + lane;
+    const bool live = vi < n_vec;
+    uint4 raw = make_uint4(0, 0, 0, 0);
+    if (live) raw = __ldg(w + vi);
+    const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[2 * j] = bf16_bits_to_f32(words[j] & 0xFFFFu);
+      v[2 * j + 1] = bf16_bits_to_f32(words[j] >> 16);
+    }
+    float w_max = -INFINITY, w_min = INFINITY;
+    if (live) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        w_max = mlx_max(w_max, v[j]);
+        w_min = mlx_min(w_min, v[j]);
+      }
+    }
+#pragma unroll
+    for (int off = 1; off < LANES; off <<= 1) {
+      w_max = mlx_max(w_max, __shfl_xor_sync(0xffffffffu, w_max, off));
+      w_min = mlx_min(w_min, __shfl_xor_sync(0xffffffffu, w_min, off));
+    }
+    const bool side = fabsf(w_min) > fabsf(w_max);
+    float scale = mlx_max(__fdiv_rn(__fsub_rn(w_max, w_min), n_bins), eps);
+    scale = side ? scale : -scale;
+    const float edge = side ? w_min : w_max;
+    const float q0 = rintf(__fdiv_rn(edge, scale));
+    float bias = 0.0f;
+    if (q0 != 0.0f) {
+      scale = __fdiv_rn(edge, q0);
+      bias = edge;
+    }
+    uint32_t packed[BITS / 4] = {};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float q = rintf(__fdiv_rn(__fsub_rn(v[j], bias), scale));
+      q = mlx_min(mlx_max(q, 0.0f), n_bins);
+      const uint32_t code = (q == q) ? static_cast<uint32_t>(q) : 0u;
+      if constexpr (BITS == 4) {
+        packed[0] |= code << (4 * j);
+      } else {
+        packed[j >> 2] |= code << (8 * (j & 3));
+      }
+    }
+    if (live) {
+      if constexpr (BITS == 4) {
+        codes[vi] = packed[0];
+      } else {
+        reinterpret_cast<uint2*>(codes)[vi] = make_uint2(packed[0], packed[1]);
+      }
+      if ((lane & (LANES - 1)) == 0) {
+        const int64_t gi = vi / LANES;
+        scales[gi] = f32_to_bf16_bits(scale);
+        biases[gi] = f32_to_bf16_bits(bias);
+      }
+    }
+  }
+}
+
+// One thread = 4 code words.  4-bit: 32 elements (64 B out); 8-bit: 16 (32 B).
+template <int BITS>
+__global__ void __launch_bounds__(256) dequantize_kernel(const uint4* __restrict__ codes,
+                                                         int64_t n_quads, int group_shift,
+                                                         const uint16_t* __restrict__ scales,
+                                                         const uint16_t* __restrict__ biases,
+                                                         uint4* __restrict__ out) {
+  constexpr int kElems = 4 * 32 / BITS;  // elements per thread
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t qi = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; qi < n_quads;
+       qi += stride) {
+    const uint4 c = __ldg(codes + qi);
+    const int64_t first = qi * kElems;       // flat element index (group never straddled)
+    const int64_t gi = first >> group_shift;
+    const uint32_t s2 = bf16_dup(__ldg(scales + gi));
+    const uint32_t b2 = bf16_dup(__ldg(biases + gi));
+    const uint32_t words[4] = {c.x, c.y, c.z, c.w};
+    if constexpr (BITS == 4) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t o[4];
+        dequant_u4x8(words[j], s2, b2, o);
+        out[qi * 4 + j] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        uint32_t o0[2], o1[2];
+        dequant_u8x4(words[2 * j], s2, b2, o0);
+        dequant_u8x4(words[2 * j + 1], s2, b2, o1);
+        out[qi * 2 + j] = make_uint4(o0[0], o0[1], o1[0], o1[1]);
+      }
+    }
+  }
+}
+
+int check_qargs(int64_t rows, int64_t cols, int group_size, int bits) {
+  if (bits != 4 && bits != 8) return fail(TQ_ERR_UNSUPPORTED, "bits must be 4 or 8, got %d", bits);
+  if (group_size != 32 && group_size != 64 && group_size != 128)
+    return fail(TQ_ERR_UNSUPPORTED, "group_size must be 32, 64 or 128, got %d", group_size);
+  if (rows < 0 || cols < 0) return fail(TQ_ERR_INVALID, "negative shape [%lld, %lld]",
+                                        (long long)rows, (long long)cols);
+  if (cols % group_size != 0)
+    return fail(TQ_ERR_INVALID,
+                "the last dimension (%lld) must be divisible by the quantization group size (%d)",
+                (long long)cols, group_size);
+  return TQ_OK;
+}
+
+int grid_for(int64_t work_items, int block) {
+  const int64_t want = (work_items + block - 1) / block;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+  return static_cast<int>(want < 1 ? 1 : (want > cap ? cap : want));
+}
+
+}  // namespace
+}  // namespace tq
+
+extern "C" int tq_quantize(const void* w, int64_t rows, int64_t cols, int group_size, int bits,
+                           void* codes, void* scales, void* biases, void* stream) {
+  using namespace tq;
+  int rc = check_qargs(rows, cols, group_size, bits);
+  if (rc) return rc;
+  if (rows == 0 || cols == 0) return TQ_OK;
+  if (!w || !codes || !scales || !biases) return fail(TQ_ERR_INVALID, "null pointer");
+  if (!aligned(w, 16) || !aligned(codes, 16))
+    return fail(TQ_ERR_MISALIGNED, "w and codes must be 16-byte aligned");
+  if (!aligned(scales, 2) || !aligned(biases, 2))
+    return fail(TQ_ERR_MISALIGNED, "scales and biases must be 2-byte aligned");
+  const int64_t n_vec = rows * cols / 8;
+  const int block = 256;
+  const int grid = grid_for(n_vec, block);
+  cudaStream_t s = as_stream(stream);
+  const uint4* wv = static_cast<const uint4*>(w);
+  uint32_t* c = static_cast<uint32_t*>(codes);
+  uint16_t* sc = static_cast<uint16_t*>(scales);
+  uint16_t* bi = static_cast<uint16_t*>(biases);
+  const int lanes = group_size / 8;
+  if (bits == 4) {
+    if (lanes == 4) quantize_kernel<4, 4><<<grid, block, 0, s>>>(wv, n_vec, c, sc, bi);
+    else if (lanes == 8) quantize_kernel<4, 8><<<grid, block, 0, s>>>(wv, n_vec, c, sc, bi);
+    else quantize_kernel<4, 16><<<grid, block, 0, s>>>(wv, n_vec, c, sc, bi);
+  } else {
+    if (lanes == 4) quantize_kernel<8, 4><<<grid, block, 0, s>>>(wv, n_vec, c, sc, bi);
+    else if (lanes == 8) quantize_kernel<8, 8><<<grid, block, 0, s>>>(wv, n_vec, c, sc, bi);
+    else quantize_kernel<8, 16><<<grid, block, 0, s>>>(wv, n_vec, c, sc, bi);
+  }
+  return check_cuda(cudaGetLastError(), "quantize launch");
+}
+
+extern "C" int tq_dequantize(const void* codes, const void* scales, const void* biases,
+                             int64_t rows, int64_t cols, int group_size, int bits, void* w,
+                             void* stream) {
+  using namespace tq;
+  int rc = check_qargs(rows, cols, group_size, bits);
+  if (rc) return rc;
+  if (rows == 0 || cols == 0) return TQ_OK;
+  if (!w || !codes || !scales || !biases) return fail(TQ_ERR_INVALID, "null pointer");
+  if (!aligned(w, 16) || !aligned(codes, 16))
+    return fail(TQ_ERR_MISALIGNED, "w and codes must be 16-byte aligned");
+  const int64_t n_words = rows * cols * bits / 32;
+  const int64_t n_quads = n_words / 4;  // cols % 32 == 0 so n_words % 4 == 0
+  const int block = 256;
+  const int grid = grid_for(n_quads, block);
+  const int shift = group_size == 32 ? 5 : (group_size == 64 ? 6 : 7);
+  cudaStream_t s = as_stream(stream);
+  if (bits == 4)
+    dequantize_kernel<4><<<grid, block, 0, s>>>(
+        static_cast<const uint4*>(codes), n_quads, shift, static_cast<const uint16_t*>(scales),
+        static_cast<const uint16_t*>(biases), static_cast<uint4*>(w));
+  else
+    dequantize_kernel<8><<<grid, block, 0, s>>>(
+        static_cast<const uint4*>(codes), n_quads, shift, static_cast<const uint16_t*>(scales),
+        static_cast<const uint16_t*>(biases), static_cast<uint4*>(w));
+  return check_cuda(cudaGetLastError(), "dequantize launch");
+}

@@ -1,0 +1,285 @@
+"""The quantized-weight ops, with MLX's names and argument meaning.
+
+``quantize``, ``dequantize`` and ``quantized_matmul`` take and return torch
+CUDA tensors (torch is only the device-memory and stream plumbing here) and
+run the hand-written sm_100a kernels of libtorobi_b200.so through its C ABI.
+Invalid arguments raise ``ValueError`` before anything is launched, as MLX's
+ops do; a failure inside the library raises ``TqError``.
+
+Reference: the engine would reach these through mlx-c (engine/src/mlxc/ops.rs);
+the LoRA-adapted linear they serve is lib/torobi/dsl/layers.rb:16-25 with
+lib/torobi/lora.rb:79-85.
+"""
+from __future__ import annotations
+
+import torch
+
+from ._lib import check, lib
+
+SUPPORTED_BITS = (4, 8)
+SUPPORTED_GROUPS = (32, 64, 128)
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _need_cuda(op: str, **tensors) -> None:
+    for name, t in tensors.items():
+        if t is None:
+            continue
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"[{op}] {name} must be a torch.Tensor")
+        if not t.is_cuda:
+            raise ValueError(f"[{op}] {name} must live on a CUDA device (there is no CPU path)")
+
+
+def _check_bits_group(op: str, group_size: int, bits: int) -> None:
+    if bits not in SUPPORTED_BITS:
+        raise ValueError(f"[{op}] {bits}-bit quantization is not supported; bits must be 4 or 8")
+    if group_size not in SUPPORTED_GROUPS:
+        raise ValueError(
+            f"[{op}] group size {group_size} is not supported; use 32, 64 or 128")
+
+
+def quantize(w: torch.Tensor, group_size: int = 64, bits: int = 4):
+    """Affine-quantize ``w`` along its last axis.
+
+    Returns ``(w_q, scales, biases)``: ``w_q`` uint32 [..., cols*bits/32] with
+    codes packed low bits first, ``scales``/``biases`` bf16 [..., cols/group].
+    """
+    op = "quantize"
+    _need_cuda(op, w=w)
+    _check_bits_group(op, group_size, bits)
+    if w.dim() < 2:
+        raise ValueError(f"[{op}] the matrix to quantize needs at least 2 dimensions, got {w.dim()}")
+    if w.dtype != torch.bfloat16:
+        raise ValueError(f"[{op}] w must be bfloat16, got {w.dtype}")
+    cols = w.shape[-1]
+    if cols % group_size != 0:
+        raise ValueError(
+            f"[{op}] the last dimension ({cols}) must be divisible by the group size "
+            f"{group_size}; w has shape {tuple(w.shape)}")
+    w2 = w.contiguous().reshape(-1, cols)
+    rows = w2.shape[0]
+    lead = tuple(w.shape[:-1])
+    codes = torch.empty(lead + (cols * bits // 32,), dtype=torch.uint32, device=w.device)
+    scales = torch.empty(lead + (cols // group_size,), dtype=torch.bfloat16, device=w.device)
+    biases = torch.empty_like(scales)
+    with torch.cuda.device(w.device):
+        check(lib().tq_quantize(_ptr(w2), rows, cols, group_size, bits, _ptr(codes), _ptr(scales),
+                                _ptr(biases), _stream()))
+    return codes, scales, biases
+
+
+def _check_packed(op: str, w_q, scales, biases, group_size: int, bits: int):
+    if w_q.dtype != torch.uint32:
+        raise ValueError(f"[{op}] the packed weight must be uint32, got {w_q.dtype}")
+    if scales.dtype != torch.bfloat16 or biases.dtype != torch.bfloat16:
+        raise ValueError(f"[{op}] scales and biases must be bfloat16")
+    cols = w_q.shape[-1] * 32 // bits
+    if cols % group_size != 0:
+        raise ValueError(f"[{op}] {cols} unpacked columns are not a whole number of groups of "
+                         f"{group_size}")
+    want = tuple(w_q.shape[:-1]) + (cols // group_size,)
+    if tuple(scales.shape) != want or tuple(biases.shape) != want:
+        raise ValueError(f"[{op}] scales and biases must have shape {want} for a packed weight "
+                         f"of shape {tuple(w_q.shape)}; got {tuple(scales.shape)} and "
+                         f"{tuple(biases.shape)}")
+    return cols
+
+
+def dequantize(w_q: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+               group_size: int = 64, bits: int = 4) -> torch.Tensor:
+    """bf16 [..., cols] with w = RNE(scale * q + bias)."""
+    op = "dequantize"
+    _need_cuda(op, w_q=w_q, scales=scales, biases=biases)
+    _check_bits_group(op, group_size, bits)
+    if w_q.dim() < 2:
+        raise ValueError(f"[{op}] the packed matrix needs at least 2 dimensions")
+    cols = _check_packed(op, w_q, scales, biases, group_size, bits)
+    lead = tuple(w_q.shape[:-1])
+    rows = 1
+    for d in lead:
+        rows *= d
+    out = torch.empty(lead + (cols,), dtype=torch.bfloat16, device=w_q.device)
+    with torch.cuda.device(w_q.device):
+        check(lib().tq_dequantize(_ptr(w_q.contiguous()), _ptr(scales.contiguous()),
+                                  _ptr(biases.contiguous()), rows, cols, group_size, bits,
+                                  _ptr(out), _stream()))
+    return out
+
+
+def _gemm_operands(op, x, w_q, scales, biases, transpose, group_size, bits):
+    _need_cuda(op, x=x, w_q=w_q, scales=scales, biases=biases)
+    _check_bits_group(op, group_size, bits)
+    if w_q.dim() != 2:
+        raise ValueError(f"[{op}] the packed weight must be 2-D, got shape {tuple(w_q.shape)}")
+    if x.dtype != torch.bfloat16:
+        raise ValueError(f"[{op}] x must be bfloat16, got {x.dtype}")
+    w_cols = _check_packed(op, w_q, scales, biases, group_size, bits)
+    w_rows = w_q.shape[0]
+    k_in = w_cols if transpose else w_rows
+    n_out = w_rows if transpose else w_cols
+    if x.shape[-1] != k_in:
+        raise ValueError(
+            f"[{op}] the last dimension of x ({x.shape[-1]}) does not match the weight: "
+            f"expected {k_in} for a [{w_rows}, {w_cols}] weight with transpose={transpose}")
+    if w_rows % 8 != 0:
+        raise ValueError(f"[{op}] the weight's row count ({w_rows}) must be a multiple of 8")
+    x2 = x.contiguous().reshape(-1, k_in)
+    return x2, w_rows, w_cols, n_out
+
+
+def quantized_matmul(x: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor,
+                     biases: torch.Tensor, transpose: bool = True, group_size: int = 64,
+                     bits: int = 4) -> torch.Tensor:
+    """``x . dequant(W)^T`` (transpose) or ``x . dequant(W)``, bf16 out."""
+    op = "quantized_matmul"
+    x2, w_rows, w_cols, n_out = _gemm_operands(op, x, w_q, scales, biases, transpose,
+                                               group_size, bits)
+    y = torch.empty(tuple(x.shape[:-1]) + (n_out,), dtype=torch.bfloat16, device=x.device)
+    with torch.cuda.device(x.device):
+        check(lib().tq_quantized_matmul(_ptr(x2), _ptr(w_q.contiguous()), _ptr(scales.contiguous()),
+                                        _ptr(biases.contiguous()), x2.shape[0], w_rows, w_cols,
+                                        1 if transpose else 0, group_size, bits, _ptr(y),
+                                        _stream()))
+    return y
+
+
+def qlora_matmul(x: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+                 transpose: bool = True, group_size: int = 64, bits: int = 4,
+                 bias: torch.Tensor | None = None, lora_up: torch.Tensor | None = None,
+                 lora_down: torch.Tensor | None = None) -> torch.Tensor:
+    """quantized_matmul plus bias and the LoRA up-projection in one kernel.
+
+    transpose: y = x W^T + bias + lora_down . lora_up^T   (lora_up = B [n, r])
+    otherwise: y = x W + lora_down . lora_up               (lora_up = A [r, k])
+    ``lora_down`` is the [m, r] bf16 down-projection already scaled by alpha/r.
+    """
+    op = "qlora_matmul"
+    x2, w_rows, w_cols, n_out = _gemm_operands(op, x, w_q, scales, biases, transpose,
+                                               group_size, bits)
+    _need_cuda(op, bias=bias, lora_up=lora_up, lora_down=lora_down)
+    rank = 0
+    if lora_up is not None or lora_down is not None:
+        if lora_up is None or lora_down is None:
+            raise ValueError(f"[{op}] lora_up and lora_down go together")
+        rank = lora_down.shape[-1]
+        want_up = (w_rows, rank) if transpose else (rank, w_cols)
+        if tuple(lora_up.shape) != want_up:
+            raise ValueError(f"[{op}] lora_up must have shape {want_up}, got {tuple(lora_up.shape)}")
+        if lora_down.reshape(-1, rank).shape[0] != x2.shape[0]:
+            raise ValueError(f"[{op}] lora_down must have one row per row of x")
+        if lora_up.dtype != torch.bfloat16 or lora_down.dtype != torch.bfloat16:
+            raise ValueError(f"[{op}] LoRA operands must be bfloat16")
+        if rank not in (8, 16):
+            raise ValueError(f"[{op}] LoRA rank must be 8 or 16, got {rank}")
+    if bias is not None:
+        if not transpose:
+            raise ValueError(f"[{op}] a bias is only defined with transpose=True")
+        if tuple(bias.shape) != (n_out,) or bias.dtype != torch.bfloat16:
+            raise ValueError(f"[{op}] bias must be bfloat16 of shape ({n_out},)")
+    y = torch.empty(tuple(x.shape[:-1]) + (n_out,), dtype=torch.bfloat16, device=x.device)
+    up = lora_up.contiguous() if lora_up is not None else None
+    down = lora_down.contiguous().reshape(-1, rank) if lora_down is not None else None
+    b = bias.contiguous() if bias is not None else None
+    with torch.cuda.device(x.device):
+        check(lib().tq_qlora_matmul(_ptr(x2), _ptr(w_q.contiguous()), _ptr(scales.contiguous()),
+                                    _ptr(biases.contiguous()), x2.shape[0], w_rows, w_cols,
+                                    1 if transpose else 0, group_size, bits, _ptr(b), _ptr(up),
+                                    _ptr(down), rank, _ptr(y), _stream()))
+    return y
+
+
+def lora_down(x: torch.Tensor, a: torch.Tensor, scale: float, want_transposed: bool = True):
+    """Scaled LoRA down-projection on the tensor cores.
+
+    Returns ``(out, out_t)``: ``out`` = RNE(scale * x . a^T) bf16 [m, r] and
+    ``out_t`` the same transposed, bf16 [r, ld] with ld = m rounded up to 8
+    (columns m.. unused), or None.
+    """
+    op = "lora_down"
+    _need_cuda(op, x=x, a=a)
+    if x.dtype != torch.bfloat16 or a.dtype != torch.bfloat16:
+        raise ValueError(f"[{op}] x and a must be bfloat16")
+    rank, k = a.shape
+    if rank not in (8, 16):
+        raise ValueError(f"[{op}] LoRA rank must be 8 or 16, got {rank}")
+    if x.shape[-1] != k:
+        raise ValueError(f"[{op}] x's last dimension ({x.shape[-1]}) must be {k}")
+    x2 = x.contiguous().reshape(-1, k)
+    m = x2.shape[0]
+    ld = (m + 7) // 8 * 8
+    out = torch.empty((m, rank), dtype=torch.bfloat16, device=x.device)
+    out_t = torch.empty((rank, ld), dtype=torch.bfloat16, device=x.device) if want_transposed else None
+    with torch.cuda.device(x.device):
+        check(lib().tq_lora_down(_ptr(x2), _ptr(a.contiguous()), m, k, rank, float(scale),
+                                 _ptr(out), _ptr(out_t), ld, _stream()))
+    return out, out_t
+
+
+def lora_grad(x: torch.Tensor, p_t: torch.Tensor, out_layout: int, out: torch.Tensor | None = None,
+              accumulate: bool = False) -> torch.Tensor:
+    """f32 LoRA weight gradient reduced over the rows of x.
+
+    ``p_t`` is [r, ld] (``lora_down``'s transposed output, ld >= rows of x).
+    layout 0 -> [c, r] = x^T p;  layout 1 -> [r, c] = p^T x.
+    """
+    op = "lora_grad"
+    _need_cuda(op, x=x, p_t=p_t, out=out)
+    rank, ld = p_t.shape
+    c = x.shape[-1]
+    x2 = x.contiguous().reshape(-1, c)
+    m = x2.shape[0]
+    if ld < m or not p_t.is_contiguous():
+        raise ValueError(f"[{op}] p_t must be contiguous with at least {m} columns, got {tuple(p_t.shape)}")
+    shape = (c, rank) if out_layout == 0 else (rank, c)
+    if out is None:
+        out = torch.empty(shape, dtype=torch.float32, device=x.device)
+        accumulate = False
+    elif tuple(out.shape) != shape or out.dtype != torch.float32 or not out.is_contiguous():
+        raise ValueError(f"[{op}] out must be a contiguous float32 tensor of shape {shape}")
+    with torch.cuda.device(x.device):
+        check(lib().tq_lora_grad(_ptr(x2), _ptr(p_t), ld, m, c, rank, out_layout,
+                                 1 if accumulate else 0, _ptr(out), _stream()))
+    return out
+
+
+def sumsq(x: torch.Tensor, out: torch.Tensor, accumulate: bool = False) -> torch.Tensor:
+    _need_cuda("sumsq", x=x, out=out)
+    with torch.cuda.device(x.device):
+        check(lib().tq_sumsq(_ptr(x), x.numel(), _ptr(out), 1 if accumulate else 0, _stream()))
+    return out
+
+
+def adamw_(params: torch.Tensor, grads: torch.Tensor, m: torch.Tensor, v: torch.Tensor, t: int,
+           lr: float, beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8,
+           weight_decay: float = 0.0, grad_scale: float = 1.0,
+           norm_sq: torch.Tensor | None = None, clip: float | None = None,
+           params_bf16: torch.Tensor | None = None) -> None:
+    """In-place AdamW step over flat f32 buffers (engine/src/optimizer.rs:305-352)."""
+    _need_cuda("adamw", params=params, grads=grads, m=m, v=v, norm_sq=norm_sq,
+               params_bf16=params_bf16)
+    n = params.numel()
+    for name, tt in (("grads", grads), ("m", m), ("v", v)):
+        if tt.numel() != n or tt.dtype != torch.float32:
+            raise ValueError(f"[adamw] {name} must be float32 with {n} elements")
+    with torch.cuda.device(params.device):
+        check(lib().tq_adamw(_ptr(params), _ptr(grads), _ptr(m), _ptr(v), n, int(t), lr, beta1,
+                             beta2, eps, weight_decay, grad_scale, _ptr(norm_sq),
+                             float(clip) if clip else 0.0, _ptr(params_bf16), _stream()))
+
+
+def transpose_to_bf16(src: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    _need_cuda("transpose_to_bf16", src=src, out=out)
+    rows, cols = src.shape
+    if out is None:
+        out = torch.empty((cols, rows), dtype=torch.bfloat16, device=src.device)
+    with torch.cuda.device(src.device):
+        check(lib().tq_transpose_to_bf16(_ptr(src.contiguous()), rows, cols, _ptr(out), _stream()))
+    return out
