@@ -1,0 +1,529 @@
+#!/usr/bin/env python
+"""QLoRA training throughput on B200: tokens/s of the data-parallel step.
+
+Workload (default): a Llama-3-8B-shaped causal LM (32 layers, hidden 4096,
+32/8 heads of 128, SwiGLU 14336, vocab 128256, RoPE theta 5e5), random init,
+every block linear quantized 4-bit group 64, LoRA rank 16 alpha 32 on all
+seven projections, bf16 activations, f32 cross-entropy, AdamW on the adapter.
+Global batch 32 x 2048 uniform random token ids, sharded over the ranks
+(strong scaling: the global batch is fixed), micro-batches of 4 sequences.
+
+    python bench.py [--gpus N --steps K --warmup W]          # this package
+    python bench.py --impl reference [...]                    # the CPU port
+
+One JSON line on rank 0.  ``value``: tokens/s over the K timed steps with the
+token ids already on the device; ``e2e``: the same through the public API with
+the ids copied from pinned host memory and the loss read back every step.
+``roofline``: the quantized GEMM (the dominant kernel) timed live with CUDA
+events around each launch on its stream, against the measured sustained bf16
+tensor peak.  ``cpu_baseline``: the CPU oracle on a bounded sample.
+
+Kernel workloads (one GPU): ``--workload qmm`` (one quantized_matmul shape),
+``qmm-sweep`` (M x projection shapes, forward and dX) and ``quant-sweep``
+(quantize/dequantize over every Qwen2.5-0.5B-shaped linear).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+METRIC = "QLoRA train tokens/s at 1/2/4/8 B200; int4 qmatmul TFLOP/s and % of roofline"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=6)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--workload", choices=("llama3-8b", "qwen2.5-0.5b", "qmm", "qmm-sweep",
+                                          "quant-sweep"), default="llama3-8b")
+    p.add_argument("--m", type=int, default=16384, help="qmm: tokens")
+    p.add_argument("--n", type=int, default=4096, help="qmm: weight rows (out features)")
+    p.add_argument("--k", type=int, default=4096, help="qmm: weight cols (in features)")
+    p.add_argument("--direction", choices=("fwd", "dx"), default="fwd")
+    p.add_argument("--global-batch", type=int, default=None)
+    p.add_argument("--seq", type=int, default=None)
+    p.add_argument("--micro-batch", type=int, default=None)
+    p.add_argument("--layers", type=int, default=None,
+                   help="override the layer count (profiling runs only)")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def workload(args):
+    import dataclasses
+
+    from torobi_b200.model import PRESETS
+
+    cfg = PRESETS[args.workload]
+    if args.layers:
+        cfg = dataclasses.replace(cfg, layers=args.layers)
+    if args.workload == "llama3-8b":
+        gb, seq, mb = 32, 2048, 4
+    else:
+        gb, seq, mb = 8, 512, 8
+    return cfg, args.global_batch or gb, args.seq or seq, args.micro_batch or mb
+
+
+def measured_peaks():
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        try:
+            return json.loads(f.read_text()), "measured"
+        except Exception:
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ----------------------------------------------------------- clocks ------
+
+class ClockSampler:
+    """nvidia-smi sampled every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock samples"]}
+
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+
+        sm = sorted(x for x in (num(r[1]) for r in rows) if x is not None)
+        mx = max((x for x in (num(r[2]) for r in rows) if x is not None), default=None)
+        power = [x for x in (num(r[3]) for r in rows) if x is not None]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = [n for i, n in enumerate(names) if any(r[5 + i].lower() == "active" for r in rows)]
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx,
+                "reasons": reasons, "samples": len(rows),
+                "power_w_max": max(power) if power else None}
+
+
+# ------------------------------------------------------- CPU baseline -----
+
+def cpu_port_tokens_per_s(cfg, tokens: int, reps: int = 1):
+    """The CPU oracle's QLoRA step work for ``tokens`` tokens through one
+    block's seven linears (forward quantized GEMM + its VJP, and the LoRA
+    branch with its weight gradients), scaled to the whole model's block
+    linears.  An upper bound on CPU tokens/s: attention, norms, the head and
+    the loss are not counted."""
+    import numpy as np
+
+    from oracle import oracle as O
+
+    rng = np.random.default_rng(7)
+    shapes = cfg.linear_shapes()
+    qw = {}
+    for name, (d_out, d_in) in shapes.items():
+        w = O.normal_bf16(rng, (d_out, d_in), 0.02)
+        qw[name] = O.quantize(w, cfg.bits, cfg.group)
+    xs = {name: O.normal_bf16(rng, (tokens, d_in)) for name, (d_out, d_in) in shapes.items()}
+    dys = {name: O.normal_bf16(rng, (tokens, d_out)) for name, (d_out, d_in) in shapes.items()}
+    r = cfg.lora_rank
+    lora = {name: (O.normal_bf16(rng, (r, d_in), 0.125), O.normal_bf16(rng, (d_out, r), 0.01))
+            for name, (d_out, d_in) in shapes.items() if name in cfg.lora_targets}
+    f = O.f32_from_bf16
+    best = float("inf")
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        for name in shapes:
+            c, s, b = qw[name]
+            if name in lora:
+                a, bl = lora[name]
+                O.qlora_linear_fwd(f(xs[name]), c, s, b, f(a), f(bl), cfg.lora_alpha / r,
+                                   cfg.bits, cfg.group)
+                O.qlora_linear_bwd(f(xs[name]), f(dys[name]), c, s, b, f(a), f(bl),
+                                   cfg.lora_alpha / r, cfg.bits, cfg.group)
+            else:
+                O.qmm_fwd(xs[name], c, s, b, cfg.bits, cfg.group)
+                O.qmm_dx(dys[name], c, s, b, cfg.bits, cfg.group)
+        best = min(best, time.perf_counter() - t0)
+    return tokens / (best * cfg.layers), best, O.num_threads()
+
+
+CPU_SAMPLE_TOKENS = 16
+
+
+def cpu_sample_text(cfg, per_layer):
+    return (f"{CPU_SAMPLE_TOKENS} tokens through one block's 7 quantized linears (forward, "
+            f"input gradient, LoRA branch and its weight gradients) on the CPU oracle, "
+            f"{per_layer:.2f} s per layer, scaled to {cfg.layers} layers; attention, norms, "
+            f"head and loss not counted")
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    cfg, gb, seq, mb = workload(args)
+    vals = []
+    per_layer = 0.0
+    cores = 1
+    for i in range(args.warmup + args.steps):
+        tps, per_layer, cores = cpu_port_tokens_per_s(cfg, CPU_SAMPLE_TOKENS)
+        if i >= args.warmup:
+            vals.append(tps)
+    v = sum(vals) / len(vals)
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * CPU_SAMPLE_TOKENS / v, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{args.workload} QLoRA train step (CPU oracle port)",
+                   "global_batch": gb, "seq_len": seq},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": cpu_sample_text(cfg, per_layer)},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+    return 0
+
+
+# -------------------------------------------------------------- ours -------
+
+def run_ours(args):
+    import torch
+
+    from torobi_b200 import ops
+    from torobi_b200.model import QLoRACausalLM
+    from torobi_b200.train import AdamWConfig, NcclGradReduce, Trainer, dist_env, shard_rows
+
+    rank, world, local = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE is {world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    cfg, gb, seq, mb = workload(args)
+    lo, hi = shard_rows(gb, world, rank)
+    rows = hi - lo
+    if rows % mb:
+        mb = rows
+    model = QLoRACausalLM(cfg, dev, seed=1234)
+    store = dist.distributed_c10d._get_default_store() if dist else None
+    reduce = NcclGradReduce(rank, world, store)
+    trainer = Trainer(model, AdamWConfig(lr=1e-4), micro_batch=mb, reduce=reduce, rank=rank,
+                      world=world)
+    K, W = args.steps, args.warmup
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1000 + rank)
+    ids_dev = torch.randint(0, cfg.vocab, (W + K, rows, seq), generator=gen, device=dev)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if not dist:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for i in range(W):
+        trainer.step(ids_dev[i])
+        trainer.settle()
+    barrier()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    rec = ops.LaunchRecorder(timed=("qmm",))
+    ops.set_recorder(rec)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for i in range(K):
+        trainer.step(ids_dev[W + i])
+    ev1.record()
+    torch.cuda.synchronize()
+    ops.set_recorder(None)
+    clk = clocks.stop()
+    local_ms = ev0.elapsed_time(ev1)
+    ms = max_over_ranks(local_ms)
+    loss = float(trainer.loss_buf.item())
+    trainer.settle()
+    tokens_per_step = gb * seq
+    value = tokens_per_step * K / (ms / 1000.0)
+    summ = rec.summary().get("qmm", {"launches": 0, "ms": 0.0, "flops": 0.0})
+    launches = rec.launches()
+
+    e2e = None
+    if not args.no_e2e:
+        gen_h = torch.Generator()
+        gen_h.manual_seed(2000 + rank)
+        ids_host = torch.randint(0, cfg.vocab, (K, rows, seq), generator=gen_h).pin_memory()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(K):
+            ids = ids_host[i].to(dev, non_blocking=True)
+            trainer.step(ids)
+            trainer.settle()                      # gradient norm read back (the step's outcome)
+            _ = float(trainer.loss_buf.item())    # loss read back
+        e1.record()
+        torch.cuda.synchronize()
+        ms_e2e = max_over_ranks(e0.elapsed_time(e1))
+        e2e = {"value": tokens_per_step * K / (ms_e2e / 1000.0), "unit": "tokens/s",
+               "h2d_bytes_per_step": rows * seq * ids_host.element_size() * world,
+               "d2h_bytes_per_step": 8 * world}
+
+    peaks, peak_kind = measured_peaks()
+    achieved = summ["flops"] / (summ["ms"] / 1000.0) / 1e12 if summ["ms"] > 0 else 0.0
+    peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    roofline = {
+        "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+        "frac": achieved / peak if peak else None, "traffic": None,
+        "kernel": "qmm_kernel (tcgen05 quantized_matmul, forward and dX, fused LoRA)",
+        "peak_kind": f"{peak_kind} sustained bf16 (cuBLAS, long loop)",
+        "launches_timed": int(summ["launches"]),
+        "share_of_step": summ["ms"] / max(1e-9, local_ms),
+    }
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tps, per_layer, cores = cpu_port_tokens_per_s(cfg, CPU_SAMPLE_TOKENS)
+        cpu = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": cpu_sample_text(cfg, per_layer)}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (uniform random token ids, random-init weights)",
+            "config": {"workload": f"{args.workload} QLoRA train step", "global_batch": gb,
+                       "seq_len": seq, "micro_batch": mb, "parallelism": f"dp{world}",
+                       "layers": cfg.layers, "quant": f"{cfg.bits}-bit g{cfg.group}",
+                       "lora": f"r{cfg.lora_rank} a{int(cfg.lora_alpha)} on "
+                               f"{'+'.join(cfg.lora_targets)}",
+                       "l2": "inputs larger than L2 (quantized base weights "
+                             f"{model.base_nbytes() / 1e9:.2f} GB read per step)"},
+            "model_tflops_per_s": value * cfg.flops_per_token(seq) / 1e12,
+            "loss": loss,
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    reduce.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+# ------------------------------------------------------ kernel workloads ---
+
+# quantized_matmul shapes: Llama-3-8B projections (4096x4096, 1024x4096,
+# 14336x4096, 4096x14336) and Llama-3-70B ones (8192x8192, 28672x8192,
+# 8192x28672), as (w_rows = out features, w_cols = in features).
+QMM_SHAPES = [(4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336), (8192, 8192),
+              (28672, 8192), (8192, 28672)]
+QMM_MS = [16, 128, 1024, 4096, 16384]
+
+
+def _time_kernel(fn, iters, warmup, flush):
+    """Mean CUDA-event time of fn() with an L2 flush before every launch;
+    the flush runs outside the timed events."""
+    import torch
+
+    for _ in range(warmup):
+        flush()
+        fn()
+    torch.cuda.synchronize()
+    total = 0.0
+    for _ in range(iters):
+        flush()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        total += s.elapsed_time(e)
+    return total / iters
+
+
+def _qmm_case(m, n, k, direction, dev, seed=0):
+    import torch
+
+    from torobi_b200 import ops
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    w = (torch.randn(n, k, device=dev, generator=g) * 0.02).bfloat16()
+    c, s, b = ops.quantize(w, 64, 4)
+    del w
+    if direction == "fwd":
+        x = torch.randn(m, k, device=dev, generator=g).bfloat16()
+        return (lambda: ops.quantized_matmul(x, c, s, b, True, 64, 4)), (x, c, s, b)
+    dy = torch.randn(m, n, device=dev, generator=g).bfloat16()
+    return (lambda: ops.quantized_matmul(dy, c, s, b, False, 64, 4)), (dy, c, s, b)
+
+
+def run_kernels(args):
+    import torch
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    flush_buf = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    flush = lambda: flush_buf.zero_()  # noqa: E731  (256 MB > 126 MB of L2)
+    peaks, peak_kind = measured_peaks()
+    burst = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    K, W = args.steps, args.warmup
+    common = {"n_gpus": 1, "steps": K, "warmup": W, "higher_is_better": True,
+              "vs_baseline": None, "data": "synthetic"}
+    if args.workload == "qmm":
+        fn, _ = _qmm_case(args.m, args.n, args.k, args.direction, dev)
+        ms = _time_kernel(fn, K, W, flush)
+        tf = 2.0 * args.m * args.n * args.k / (ms / 1000.0) / 1e12
+        print(json.dumps({"metric": "int4 quantized_matmul TFLOP/s", "value": tf,
+                          "unit": "TFLOP/s", "ms_per_step": ms, "scaling": "weak",
+                          "dtype": "bf16", **common,
+                          "config": {"workload": f"quantized_matmul {args.direction}",
+                                     "m": args.m, "w_rows": args.n, "w_cols": args.k,
+                                     "l2": "flushed before every launch"},
+                          "roofline": {"bound": "tensor", "achieved": tf, "peak": burst,
+                                       "unit": "TFLOP/s", "frac": tf / burst,
+                                       "peak_kind": f"{peak_kind} burst bf16"}}), flush=True)
+        return 0
+    if args.workload == "qmm-sweep":
+        rows = []
+        for n, k in QMM_SHAPES:
+            for m in QMM_MS:
+                for d in ("fwd", "dx"):
+                    fn, keep = _qmm_case(m, n, k, d, dev)
+                    ms = _time_kernel(fn, K, W, flush)
+                    fl = 2.0 * m * n * k
+                    byts = m * k * 2 + n * k * (0.5 + 4 / 64) + m * n * 2
+                    tf = fl / (ms / 1000.0) / 1e12
+                    gbs = byts / (ms / 1000.0) / 1e9
+                    bound = "hbm" if fl / byts < burst * 1e12 / (hbm * 1e9) else "tensor"
+                    frac = gbs / hbm if bound == "hbm" else tf / burst
+                    rows.append({"m": m, "w_rows": n, "w_cols": k, "dir": d, "ms": ms,
+                                 "tflops": tf, "gbs": gbs, "bound": bound, "frac": frac})
+                    print(json.dumps(rows[-1]), file=sys.stderr, flush=True)
+                    del keep, fn
+        big = [r["tflops"] for r in rows if r["m"] >= 4096]
+        val = sum(big) / len(big)
+        print(json.dumps({"metric": "int4 quantized_matmul TFLOP/s (mean over M>=4096)",
+                          "value": val, "unit": "TFLOP/s", "scaling": "weak", "dtype": "bf16",
+                          **common,
+                          "config": {"workload": "quantized_matmul shape sweep, 4-bit g64",
+                                     "l2": "flushed before every launch"},
+                          "roofline": {"bound": "tensor", "achieved": val, "peak": burst,
+                                       "unit": "TFLOP/s", "frac": val / burst,
+                                       "peak_kind": f"{peak_kind} burst bf16"},
+                          "sweep": rows}), flush=True)
+        return 0
+    if args.workload == "quant-sweep":
+        from torobi_b200 import ops
+        from torobi_b200.model import QWEN2_5_0_5B
+
+        shapes = list(QWEN2_5_0_5B.linear_shapes().values())
+        g = torch.Generator(device=dev)
+        g.manual_seed(0)
+        mats = [(torch.randn(o, i, device=dev, generator=g) * 0.02).bfloat16() for o, i in shapes]
+        for wm in mats:
+            mask = torch.rand(wm.shape, device=dev, generator=g) < 0.001
+            sign = torch.where(torch.rand(wm.shape, device=dev, generator=g) < 0.5, -0.5, 0.5)
+            wm[mask] = sign[mask].bfloat16()
+        # Each shape stacked over the 24 layers, so a launch is HBM-sized.
+        big = [torch.cat([wm] * QWEN2_5_0_5B.layers) for wm in mats]
+        rows = []
+        for bits in (4, 8):
+            for grp in (32, 64, 128):
+                tq_ms = tdq_ms = 0.0
+                nbytes = 0.0
+                for wm in big:
+                    tq_ms += _time_kernel(lambda: ops.quantize(wm, grp, bits), K, W, flush)
+                    c, s_, b_ = ops.quantize(wm, grp, bits)
+                    tdq_ms += _time_kernel(lambda: ops.dequantize(c, s_, b_, grp, bits), K, W,
+                                           flush)
+                    nbytes += wm.numel() * (2 + bits / 8 + 4 / grp)
+                rows.append({"bits": bits, "group": grp, "quantize_gbs": nbytes / tq_ms / 1e6,
+                             "dequantize_gbs": nbytes / tdq_ms / 1e6, "bytes": nbytes})
+                print(json.dumps(rows[-1]), file=sys.stderr, flush=True)
+        val = sum(r["dequantize_gbs"] for r in rows) / len(rows)
+        print(json.dumps({"metric": "quantize/dequantize GB/s (Qwen2.5-0.5B shapes, 24 layers)",
+                          "value": val, "unit": "GB/s", "scaling": "weak",
+                          "dtype": "u4/u8 codes, bf16", **common,
+                          "config": {"workload": "affine quantize/dequantize sweep",
+                                     "l2": "flushed before every launch"},
+                          "roofline": {"bound": "hbm", "achieved": val, "peak": hbm,
+                                       "unit": "GB/s", "frac": val / hbm,
+                                       "peak_kind": f"{peak_kind} copy"},
+                          "sweep": rows}), flush=True)
+        return 0
+    raise SystemExit(f"unknown kernel workload {args.workload}")
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    if args.workload in ("qmm", "qmm-sweep", "quant-sweep"):
+        return run_kernels(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -188,8 +188,13 @@ static inline uint32_t code_at(const uint32_t *codes_row, int64_t col, int bits)
 }
 
 static inline uint16_t dequant_one(uint32_t q, uint16_t s, uint16_t b) {
-    double v = (double)bf16_to_f32(s) * (double)q + (double)bf16_to_f32(b);
-    return f64_to_bf16(v);
+    const float sf = bf16_to_f32(s), bf = bf16_to_f32(b), qf = (float)q;
+    /* Fast path: when the f32 fma is exact it IS the exact value, and one
+       rounding of it to bf16 is the single rounding we want. */
+    const float v32 = fmaf(sf, qf, bf);
+    const double exact = (double)sf * (double)qf + (double)bf;
+    if ((double)v32 == exact) return f32_to_bf16(v32);
+    return f64_to_bf16(exact);
 }
 
 int or_dequantize(const uint32_t *codes, const uint16_t *scales, const uint16_t *biases,

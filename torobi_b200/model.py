@@ -1,0 +1,230 @@
+"""A Llama-shaped causal LM whose linears run through the quantized-weight path.
+
+The description follows the reference's lib/torobi/models/llama.rb:
+pre-norm blocks (``x += attn(norm(x)); x += mlp(norm(x))``, :263-267), GQA
+attention with RoPE on q and k and a causal mask (:285-316), SwiGLU
+``down((gate * sigmoid(gate)) * up)`` (:320-327), a final RMS norm, and a head
+that is the embedding table transposed when tied (:240-259).
+RMSNorm is ``x * rsqrt(mean(x^2) + eps) * w`` (engine/src/interp.rs:312-319);
+RoPE rotates the first half of each head against the second with angles
+``p / theta^(2i/d)`` (engine/src/interp.rs:350-388); the loss is the mean of
+``logsumexp(logits) - logits[target]`` in f32 (engine/src/interp.rs:440-444)
+over next-token targets.
+
+Every linear of every block is a ``QuantizedWeight`` (MLX affine codes) run by
+the tcgen05 quantized GEMM; adapted linears add the fused LoRA branch.  The
+glue between them (norms, RoPE, attention, SwiGLU, the bf16 head and the loss)
+is PyTorch -- it is outside the quantized-weight path this package replaces.
+The head stays bf16 (a plain library GEMM): QLoRA quantizes the blocks'
+linears and keeps the vocabulary projection in the compute dtype.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn.functional as F
+
+from .qlora import Adapter, LoRAStore, QuantizedWeight, qlora_linear
+
+LINEARS = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+
+
+@dataclass(frozen=True)
+class DecoderConfig:
+    vocab: int
+    hidden: int
+    intermediate: int
+    layers: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    rope_theta: float
+    rms_eps: float
+    tie_embeddings: bool
+    attention_bias: bool
+    bits: int = 4
+    group: int = 64
+    lora_rank: int = 8
+    lora_alpha: float = 16.0
+    lora_targets: tuple[str, ...] = ("q_proj", "v_proj")
+
+    def linear_shapes(self) -> dict[str, tuple[int, int]]:
+        """[d_out, d_in] of each block linear (PyTorch layout)."""
+        h, i = self.hidden, self.intermediate
+        q, kv = self.heads * self.head_dim, self.kv_heads * self.head_dim
+        return {"q_proj": (q, h), "k_proj": (kv, h), "v_proj": (kv, h), "o_proj": (h, q),
+                "gate_proj": (i, h), "up_proj": (i, h), "down_proj": (h, i)}
+
+    def quantized_params(self) -> int:
+        return self.layers * sum(o * i for o, i in self.linear_shapes().values())
+
+    def lora_params(self) -> int:
+        r = self.lora_rank
+        return self.layers * sum(r * (o + i) for n, (o, i) in self.linear_shapes().items()
+                                 if n in self.lora_targets)
+
+    def flops_per_token(self, seq: int) -> float:
+        """Training FLOPs per token with a frozen base: forward (2P) plus the
+        input gradient (2P) through every block linear and the head, plus
+        causal attention (forward QK^T and PV, backward twice that)."""
+        p = sum(o * i for o, i in self.linear_shapes().values()) * self.layers
+        p += self.vocab * self.hidden
+        attn_fwd = 2 * 2 * self.heads * self.head_dim * seq / 2 * self.layers
+        return 4.0 * p + 3.0 * attn_fwd
+
+
+# Qwen2.5-0.5B-shaped: hidden 896, intermediate 4864, 24 layers, 14/2 heads of 64,
+# tied 151936 vocabulary, q/k/v biases (the qwen2 family), theta 1e6.
+QWEN2_5_0_5B = DecoderConfig(vocab=151936, hidden=896, intermediate=4864, layers=24, heads=14,
+                             kv_heads=2, head_dim=64, rope_theta=1e6, rms_eps=1e-6,
+                             tie_embeddings=True, attention_bias=True, lora_rank=8,
+                             lora_alpha=16.0, lora_targets=("q_proj", "v_proj"))
+
+# Llama-3-8B-shaped: hidden 4096, intermediate 14336, 32 layers, 32/8 heads of
+# 128, untied 128256 vocabulary, theta 5e5; LoRA r16 alpha 32 on all seven.
+LLAMA3_8B = DecoderConfig(vocab=128256, hidden=4096, intermediate=14336, layers=32, heads=32,
+                          kv_heads=8, head_dim=128, rope_theta=5e5, rms_eps=1e-5,
+                          tie_embeddings=False, attention_bias=False, lora_rank=16,
+                          lora_alpha=32.0, lora_targets=LINEARS)
+
+PRESETS = {"qwen2.5-0.5b": QWEN2_5_0_5B, "llama3-8b": LLAMA3_8B}
+
+
+def tiny_config(**over) -> DecoderConfig:
+    """A small model of the same shape family, for tests."""
+    base = dict(vocab=1024, hidden=256, intermediate=512, layers=2, heads=4, kv_heads=2,
+                head_dim=64, rope_theta=1e4, rms_eps=1e-6, tie_embeddings=True,
+                attention_bias=True, lora_rank=8, lora_alpha=16.0,
+                lora_targets=("q_proj", "v_proj"))
+    base.update(over)
+    return DecoderConfig(**base)
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    scale = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return (xf * scale * w.float()).to(x.dtype)
+
+
+def rope_tables(seq: int, dim: int, theta: float, device) -> tuple[torch.Tensor, torch.Tensor]:
+    half = dim // 2
+    p = torch.arange(seq, dtype=torch.float32, device=device)[:, None]
+    i = torch.arange(half, dtype=torch.float32, device=device)[None, :]
+    angle = p / torch.pow(torch.tensor(theta, dtype=torch.float32, device=device), 2.0 * i / dim)
+    return torch.cos(angle), torch.sin(angle)
+
+
+def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """x [B, H, S, D]: the first half rotates against the second."""
+    half = x.shape[-1] // 2
+    xf = x.float()
+    a, b = xf[..., :half], xf[..., half:]
+    return torch.cat([a * cos - b * sin, b * cos + a * sin], dim=-1).to(x.dtype)
+
+
+@dataclass
+class Block:
+    input_norm: torch.Tensor
+    post_norm: torch.Tensor
+    linears: dict[str, QuantizedWeight] = field(default_factory=dict)
+    adapters: dict[str, Adapter | None] = field(default_factory=dict)
+
+
+class QLoRACausalLM:
+    """Random-init model with quantized block linears and a LoRA store."""
+
+    def __init__(self, cfg: DecoderConfig, device: torch.device | str = "cuda", seed: int = 0,
+                 dtype: torch.dtype = torch.bfloat16):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.dtype = dtype
+        gen = torch.Generator(device=self.device)
+        gen.manual_seed(seed)
+        dev = self.device
+        # Embedding table: normal std 0.02 (lib/torobi/dsl/layers.rb:30-35).
+        self.embed = (torch.randn(cfg.vocab, cfg.hidden, device=dev, generator=gen) * 0.02).to(dtype)
+        self.final_norm = torch.ones(cfg.hidden, dtype=dtype, device=dev)
+        if cfg.tie_embeddings:
+            self.lm_head = None
+        else:
+            bound = math.sqrt(6.0 / cfg.hidden)
+            self.lm_head = torch.empty(cfg.vocab, cfg.hidden, device=dev).uniform_(
+                -bound, bound, generator=gen).to(dtype)
+        self.store = LoRAStore(dev)
+        shapes = cfg.linear_shapes()
+        self.blocks: list[Block] = []
+        for li in range(cfg.layers):
+            blk = Block(torch.ones(cfg.hidden, dtype=dtype, device=dev),
+                        torch.ones(cfg.hidden, dtype=dtype, device=dev))
+            for name, (d_out, d_in) in shapes.items():
+                # Linear weights: kaiming_uniform, bound sqrt(6 / d_in)
+                # (engine/src/init.rs:42-55), quantized once at materialisation.
+                bound = math.sqrt(6.0 / d_in)
+                w = torch.empty(d_out, d_in, device=dev).uniform_(-bound, bound, generator=gen)
+                bias = None
+                if cfg.attention_bias and name in ("q_proj", "k_proj", "v_proj"):
+                    bias = torch.zeros(d_out, dtype=dtype, device=dev)
+                blk.linears[name] = QuantizedWeight.from_dense(w.to(dtype), cfg.bits, cfg.group,
+                                                               bias)
+                del w
+                if name in cfg.lora_targets:
+                    self.store.declare(f"layers.{li}.{name}", d_in, d_out, cfg.lora_rank,
+                                       cfg.lora_alpha)
+            self.blocks.append(blk)
+        self.store.materialize(gen)
+        for li, blk in enumerate(self.blocks):
+            for name in shapes:
+                blk.adapters[name] = self.store.adapters.get(f"layers.{li}.{name}")
+        self._rope_cache: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
+
+    def _rope(self, seq: int):
+        t = self._rope_cache.get(seq)
+        if t is None:
+            t = rope_tables(seq, self.cfg.head_dim, self.cfg.rope_theta, self.device)
+            self._rope_cache[seq] = t
+        return t
+
+    def block_forward(self, blk: Block, x: torch.Tensor) -> torch.Tensor:
+        cfg = self.cfg
+        B, S, H = x.shape
+        cos, sin = self._rope(S)
+        h = rms_norm(x, blk.input_norm, cfg.rms_eps)
+        q = qlora_linear(h, blk.linears["q_proj"], blk.adapters["q_proj"])
+        k = qlora_linear(h, blk.linears["k_proj"], blk.adapters["k_proj"])
+        v = qlora_linear(h, blk.linears["v_proj"], blk.adapters["v_proj"])
+        q = q.view(B, S, cfg.heads, cfg.head_dim).transpose(1, 2)
+        k = k.view(B, S, cfg.kv_heads, cfg.head_dim).transpose(1, 2)
+        v = v.view(B, S, cfg.kv_heads, cfg.head_dim).transpose(1, 2)
+        q = apply_rope(q, cos, sin)
+        k = apply_rope(k, cos, sin)
+        att = F.scaled_dot_product_attention(q, k, v, is_causal=True,
+                                             enable_gqa=cfg.heads != cfg.kv_heads)
+        att = att.transpose(1, 2).reshape(B, S, cfg.heads * cfg.head_dim)
+        x = x + qlora_linear(att, blk.linears["o_proj"], blk.adapters["o_proj"])
+        h = rms_norm(x, blk.post_norm, cfg.rms_eps)
+        g = qlora_linear(h, blk.linears["gate_proj"], blk.adapters["gate_proj"])
+        u = qlora_linear(h, blk.linears["up_proj"], blk.adapters["up_proj"])
+        a = F.silu(g) * u
+        return x + qlora_linear(a, blk.linears["down_proj"], blk.adapters["down_proj"])
+
+    def hidden(self, ids: torch.Tensor) -> torch.Tensor:
+        x = F.embedding(ids, self.embed)
+        for blk in self.blocks:
+            x = self.block_forward(blk, x)
+        return rms_norm(x, self.final_norm, self.cfg.rms_eps)
+
+    def logits(self, h: torch.Tensor) -> torch.Tensor:
+        head = self.embed if self.lm_head is None else self.lm_head
+        return h @ head.t()
+
+    def loss(self, ids: torch.Tensor) -> torch.Tensor:
+        """Mean next-token cross-entropy (f32) over positions 0..S-2."""
+        h = self.hidden(ids)[:, :-1]
+        z = self.logits(h).float()
+        tgt = ids[:, 1:]
+        return F.cross_entropy(z.reshape(-1, z.shape[-1]), tgt.reshape(-1))
+
+    def base_nbytes(self) -> int:
+        return sum(w.nbytes() for blk in self.blocks for w in blk.linears.values())

@@ -20,6 +20,54 @@ SUPPORTED_BITS = (4, 8)
 SUPPORTED_GROUPS = (32, 64, 128)
 
 
+class LaunchRecorder:
+    """Counts this library's kernel launches and, for the kinds listed in
+    ``timed``, brackets each launch with CUDA events on the launching stream
+    and accumulates the launch's algorithmic FLOPs (for the roofline)."""
+
+    def __init__(self, timed=("qmm",)):
+        self.timed = set(timed)
+        self.counts: dict[str, int] = {}
+        self.pairs: list[tuple[str, torch.cuda.Event, torch.cuda.Event, float]] = []
+
+    def launches(self) -> int:
+        return sum(self.counts.values())
+
+    def summary(self) -> dict[str, dict[str, float]]:
+        out: dict[str, dict[str, float]] = {}
+        for kind, s, e, flops in self.pairs:
+            d = out.setdefault(kind, {"launches": 0, "ms": 0.0, "flops": 0.0})
+            d["launches"] += 1
+            d["ms"] += s.elapsed_time(e)
+            d["flops"] += flops
+        return out
+
+
+_REC: LaunchRecorder | None = None
+
+
+def set_recorder(rec: LaunchRecorder | None) -> None:
+    global _REC
+    _REC = rec
+
+
+def _launch(kind: str, call, flops: float = 0.0) -> None:
+    rec = _REC
+    if rec is None:
+        check(call())
+        return
+    rec.counts[kind] = rec.counts.get(kind, 0) + 1
+    if kind in rec.timed:
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        check(call())
+        e.record()
+        rec.pairs.append((kind, s, e, flops))
+    else:
+        check(call())
+
+
 def _stream() -> int:
     return torch.cuda.current_stream().cuda_stream
 
@@ -71,8 +119,9 @@ def quantize(w: torch.Tensor, group_size: int = 64, bits: int = 4):
     scales = torch.empty(lead + (cols // group_size,), dtype=torch.bfloat16, device=w.device)
     biases = torch.empty_like(scales)
     with torch.cuda.device(w.device):
-        check(lib().tq_quantize(_ptr(w2), rows, cols, group_size, bits, _ptr(codes), _ptr(scales),
-                                _ptr(biases), _stream()))
+        _launch("quantize", lambda: lib().tq_quantize(
+            _ptr(w2), rows, cols, group_size, bits, _ptr(codes), _ptr(scales), _ptr(biases),
+            _stream()))
     return codes, scales, biases
 
 
@@ -108,9 +157,9 @@ def dequantize(w_q: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
         rows *= d
     out = torch.empty(lead + (cols,), dtype=torch.bfloat16, device=w_q.device)
     with torch.cuda.device(w_q.device):
-        check(lib().tq_dequantize(_ptr(w_q.contiguous()), _ptr(scales.contiguous()),
-                                  _ptr(biases.contiguous()), rows, cols, group_size, bits,
-                                  _ptr(out), _stream()))
+        _launch("dequantize", lambda: lib().tq_dequantize(
+            _ptr(w_q.contiguous()), _ptr(scales.contiguous()), _ptr(biases.contiguous()), rows,
+            cols, group_size, bits, _ptr(out), _stream()))
     return out
 
 
@@ -144,10 +193,10 @@ def quantized_matmul(x: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor,
                                                group_size, bits)
     y = torch.empty(tuple(x.shape[:-1]) + (n_out,), dtype=torch.bfloat16, device=x.device)
     with torch.cuda.device(x.device):
-        check(lib().tq_quantized_matmul(_ptr(x2), _ptr(w_q.contiguous()), _ptr(scales.contiguous()),
-                                        _ptr(biases.contiguous()), x2.shape[0], w_rows, w_cols,
-                                        1 if transpose else 0, group_size, bits, _ptr(y),
-                                        _stream()))
+        _launch("qmm", lambda: lib().tq_quantized_matmul(
+            _ptr(x2), _ptr(w_q.contiguous()), _ptr(scales.contiguous()), _ptr(biases.contiguous()),
+            x2.shape[0], w_rows, w_cols, 1 if transpose else 0, group_size, bits, _ptr(y),
+            _stream()), 2.0 * x2.shape[0] * w_rows * w_cols)
     return y
 
 
@@ -189,10 +238,10 @@ def qlora_matmul(x: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, biase
     down = lora_down.contiguous().reshape(-1, rank) if lora_down is not None else None
     b = bias.contiguous() if bias is not None else None
     with torch.cuda.device(x.device):
-        check(lib().tq_qlora_matmul(_ptr(x2), _ptr(w_q.contiguous()), _ptr(scales.contiguous()),
-                                    _ptr(biases.contiguous()), x2.shape[0], w_rows, w_cols,
-                                    1 if transpose else 0, group_size, bits, _ptr(b), _ptr(up),
-                                    _ptr(down), rank, _ptr(y), _stream()))
+        _launch("qmm", lambda: lib().tq_qlora_matmul(
+            _ptr(x2), _ptr(w_q.contiguous()), _ptr(scales.contiguous()), _ptr(biases.contiguous()),
+            x2.shape[0], w_rows, w_cols, 1 if transpose else 0, group_size, bits, _ptr(b), _ptr(up),
+            _ptr(down), rank, _ptr(y), _stream()), 2.0 * x2.shape[0] * w_rows * w_cols)
     return y
 
 
@@ -218,8 +267,9 @@ def lora_down(x: torch.Tensor, a: torch.Tensor, scale: float, want_transposed: b
     out = torch.empty((m, rank), dtype=torch.bfloat16, device=x.device)
     out_t = torch.empty((rank, ld), dtype=torch.bfloat16, device=x.device) if want_transposed else None
     with torch.cuda.device(x.device):
-        check(lib().tq_lora_down(_ptr(x2), _ptr(a.contiguous()), m, k, rank, float(scale),
-                                 _ptr(out), _ptr(out_t), ld, _stream()))
+        _launch("lora_down", lambda: lib().tq_lora_down(
+            _ptr(x2), _ptr(a.contiguous()), m, k, rank, float(scale), _ptr(out), _ptr(out_t), ld,
+            _stream()))
     return out, out_t
 
 
@@ -245,15 +295,17 @@ def lora_grad(x: torch.Tensor, p_t: torch.Tensor, out_layout: int, out: torch.Te
     elif tuple(out.shape) != shape or out.dtype != torch.float32 or not out.is_contiguous():
         raise ValueError(f"[{op}] out must be a contiguous float32 tensor of shape {shape}")
     with torch.cuda.device(x.device):
-        check(lib().tq_lora_grad(_ptr(x2), _ptr(p_t), ld, m, c, rank, out_layout,
-                                 1 if accumulate else 0, _ptr(out), _stream()))
+        _launch("lora_grad", lambda: lib().tq_lora_grad(
+            _ptr(x2), _ptr(p_t), ld, m, c, rank, out_layout, 1 if accumulate else 0, _ptr(out),
+            _stream()))
     return out
 
 
 def sumsq(x: torch.Tensor, out: torch.Tensor, accumulate: bool = False) -> torch.Tensor:
     _need_cuda("sumsq", x=x, out=out)
     with torch.cuda.device(x.device):
-        check(lib().tq_sumsq(_ptr(x), x.numel(), _ptr(out), 1 if accumulate else 0, _stream()))
+        _launch("sumsq", lambda: lib().tq_sumsq(_ptr(x), x.numel(), _ptr(out),
+                                                1 if accumulate else 0, _stream()))
     return out
 
 
@@ -270,9 +322,10 @@ def adamw_(params: torch.Tensor, grads: torch.Tensor, m: torch.Tensor, v: torch.
         if tt.numel() != n or tt.dtype != torch.float32:
             raise ValueError(f"[adamw] {name} must be float32 with {n} elements")
     with torch.cuda.device(params.device):
-        check(lib().tq_adamw(_ptr(params), _ptr(grads), _ptr(m), _ptr(v), n, int(t), lr, beta1,
-                             beta2, eps, weight_decay, grad_scale, _ptr(norm_sq),
-                             float(clip) if clip else 0.0, _ptr(params_bf16), _stream()))
+        _launch("adamw", lambda: lib().tq_adamw(
+            _ptr(params), _ptr(grads), _ptr(m), _ptr(v), n, int(t), lr, beta1, beta2, eps,
+            weight_decay, grad_scale, _ptr(norm_sq), float(clip) if clip else 0.0,
+            _ptr(params_bf16), _stream()))
 
 
 def transpose_to_bf16(src: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
@@ -281,5 +334,6 @@ def transpose_to_bf16(src: torch.Tensor, out: torch.Tensor | None = None) -> tor
     if out is None:
         out = torch.empty((cols, rows), dtype=torch.bfloat16, device=src.device)
     with torch.cuda.device(src.device):
-        check(lib().tq_transpose_to_bf16(_ptr(src.contiguous()), rows, cols, _ptr(out), _stream()))
+        _launch("transpose", lambda: lib().tq_transpose_to_bf16(
+            _ptr(src.contiguous()), rows, cols, _ptr(out), _stream()))
     return out

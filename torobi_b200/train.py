@@ -1,0 +1,173 @@
+"""The data-parallel QLoRA step.
+
+One process per GPU.  The quantized base is replicated, the global batch is
+sharded across ranks and split into micro-batches on each, the adapter's
+gradients accumulate in the store's flat f32 buffer, one allreduce sums them
+over ranks (NCCL through the library's C ABI), and one fused AdamW kernel
+updates every adapter on every rank identically.
+
+What a step does, and what it does when something is not finite, follows the
+reference's TrainState::advance (engine/src/state.rs:353-400): the global
+gradient norm is taken in f32 over every trained parameter; a non-finite norm
+skips the update (parameters and moments stay, the optimizer's step count does
+not move); a clip scales every gradient by clip/norm when the norm exceeds it.
+AdamW is engine/src/optimizer.rs:305-352 (defaults beta1 0.9, beta2 0.999,
+eps 1e-8, weight decay 0).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+from dataclasses import dataclass
+
+import torch
+
+from . import ops
+from ._lib import TQ_DTYPE_F32, check, lib
+
+
+# ------------------------------------------------------------ batch plan ---
+
+def shard_rows(global_rows: int, world: int, rank: int) -> tuple[int, int]:
+    """[start, stop) of this rank's rows of the global batch (equal shards)."""
+    if global_rows % world != 0:
+        raise ValueError(f"a global batch of {global_rows} rows does not shard over {world} ranks")
+    per = global_rows // world
+    return rank * per, (rank + 1) * per
+
+
+def micro_batches(rows: int, micro: int) -> list[tuple[int, int]]:
+    """Equal micro-batches of this rank's rows."""
+    if micro <= 0 or rows % micro != 0:
+        raise ValueError(f"{rows} rows do not split into micro-batches of {micro}")
+    return [(i, i + micro) for i in range(0, rows, micro)]
+
+
+def grad_scale(world: int, n_micro: int) -> float:
+    """Each micro-batch loss is a mean over its equal-sized part, so the mean
+    over the global batch is the sum of the parts over world * n_micro."""
+    return 1.0 / float(world * n_micro)
+
+
+# ------------------------------------------------------------- collective ---
+
+class NcclGradReduce:
+    """Sums a flat f32 buffer over ranks with the library's NCCL communicator.
+
+    The 128-byte NCCL id is made on rank 0 and shared through the
+    torch.distributed store (plumbing only); the allreduce itself is the C ABI.
+    """
+
+    def __init__(self, rank: int, world: int, store=None):
+        self.rank, self.world = rank, world
+        self.comm = None
+        if world == 1:
+            return
+        if store is None:
+            import torch.distributed as dist
+
+            store = dist.distributed_c10d._get_default_store()
+        idbuf = ctypes.create_string_buffer(128)
+        if rank == 0:
+            check(lib().tq_dp_unique_id(idbuf))
+            store.set("torobi_b200/nccl_id", bytes(idbuf.raw))
+        raw = store.get("torobi_b200/nccl_id")
+        ctypes.memmove(idbuf, raw, 128)
+        comm = ctypes.c_void_p()
+        check(lib().tq_dp_comm_init(ctypes.byref(comm), idbuf, world, rank))
+        self.comm = comm
+
+    def __call__(self, buf: torch.Tensor) -> None:
+        if self.world == 1:
+            return
+        assert buf.dtype == torch.float32 and buf.is_contiguous()
+        check(lib().tq_dp_allreduce_sum(self.comm, buf.data_ptr(), buf.numel(), TQ_DTYPE_F32,
+                                        torch.cuda.current_stream().cuda_stream))
+
+    def close(self) -> None:
+        if self.comm is not None:
+            check(lib().tq_dp_comm_destroy(self.comm))
+            self.comm = None
+
+
+@dataclass
+class AdamWConfig:
+    lr: float = 1e-4
+    beta1: float = 0.9
+    beta2: float = 0.999
+    eps: float = 1e-8
+    weight_decay: float = 0.0
+    clip: float | None = None
+
+
+class Trainer:
+    """Runs QLoRA steps of a ``QLoRACausalLM`` on this rank's shard."""
+
+    def __init__(self, model, opt: AdamWConfig | None = None, micro_batch: int = 1,
+                 reduce: NcclGradReduce | None = None, rank: int = 0, world: int = 1):
+        self.model = model
+        self.opt = opt or AdamWConfig()
+        self.micro = micro_batch
+        self.rank, self.world = rank, world
+        self.reduce = reduce or NcclGradReduce(rank, world)
+        self.store = model.store
+        self.norm_sq = torch.zeros(1, dtype=torch.float32, device=model.device)
+        self.loss_buf = torch.zeros(1, dtype=torch.float32, device=model.device)
+        self.t = 0          # AdamW step count (moves only when a step is taken)
+        self.steps = 0      # steps attempted
+        self.last_norm = float("nan")
+        self._pending: list[float] = []  # grad scales of launched, unsettled steps
+
+    def step(self, ids: torch.Tensor) -> torch.Tensor:
+        """One optimizer step over this rank's rows ``ids`` [rows, seq] (on
+        the device).  Returns the global mean loss as a device tensor."""
+        st = self.store
+        st.zero_grad()
+        parts = micro_batches(ids.shape[0], self.micro)
+        self.loss_buf.zero_()
+        for a, b in parts:
+            loss = self.model.loss(ids[a:b])
+            loss.backward()
+            self.loss_buf += loss.detach()
+        self.reduce(st.grads)
+        self.reduce(self.loss_buf)
+        self.loss_buf /= float(self.world * len(parts))
+        ops.sumsq(st.grads, self.norm_sq)
+        o = self.opt
+        gs = grad_scale(self.world, len(parts))
+        # The count is advanced when the step is launched and taken back in
+        # settle() if the norm turns out not finite (the kernel then moved
+        # nothing), so steps can be queued without a host sync in between.
+        self.t += 1
+        ops.adamw_(st.params, st.grads, st.m, st.v, self.t, o.lr, o.beta1, o.beta2, o.eps,
+                   o.weight_decay, grad_scale=gs, norm_sq=self.norm_sq, clip=o.clip,
+                   params_bf16=st.params16)
+        st.refresh_bf16()
+        self.steps += 1
+        self._pending.append(gs)
+        return self.loss_buf
+
+    def settle(self) -> float:
+        """Reads the last step's gradient norm (a host sync).  A non-finite norm
+        means the kernel skipped the update, so the AdamW count is taken back.
+        Call after every step when steps may be non-finite; returns the norm of
+        the averaged gradient."""
+        if self._pending:
+            gs = self._pending[-1]
+            ns = float(self.norm_sq.item())
+            if math.isfinite(ns):
+                self.last_norm = math.sqrt(ns) * gs
+            else:
+                self.t -= 1
+                self.last_norm = float("nan")
+            self._pending.clear()
+        return self.last_norm
+
+
+def dist_env() -> tuple[int, int, int]:
+    """(rank, world, local_rank) from the torchrun environment."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
