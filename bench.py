@@ -53,6 +53,7 @@ def parse_args():
     p.add_argument("--n", type=int, default=4096, help="qmm: weight rows (out features)")
     p.add_argument("--k", type=int, default=4096, help="qmm: weight cols (in features)")
     p.add_argument("--direction", choices=("fwd", "dx"), default="fwd")
+    p.add_argument("--bits", type=int, choices=(4, 8), default=4, help="qmm: code width")
     p.add_argument("--global-batch", type=int, default=None)
     p.add_argument("--seq", type=int, default=None)
     p.add_argument("--micro-batch", type=int, default=None)
@@ -401,7 +402,7 @@ def _time_kernel(fn, iters, warmup, flush):
     return total / iters
 
 
-def _qmm_case(m, n, k, direction, dev, seed=0):
+def _qmm_case(m, n, k, direction, dev, seed=0, bits=4):
     import torch
 
     from torobi_b200 import ops
@@ -409,13 +410,13 @@ def _qmm_case(m, n, k, direction, dev, seed=0):
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
     w = (torch.randn(n, k, device=dev, generator=g) * 0.02).bfloat16()
-    c, s, b = ops.quantize(w, 64, 4)
+    c, s, b = ops.quantize(w, 64, bits)
     del w
     if direction == "fwd":
         x = torch.randn(m, k, device=dev, generator=g).bfloat16()
-        return (lambda: ops.quantized_matmul(x, c, s, b, True, 64, 4)), (x, c, s, b)
+        return (lambda: ops.quantized_matmul(x, c, s, b, True, 64, bits)), (x, c, s, b)
     dy = torch.randn(m, n, device=dev, generator=g).bfloat16()
-    return (lambda: ops.quantized_matmul(dy, c, s, b, False, 64, 4)), (dy, c, s, b)
+    return (lambda: ops.quantized_matmul(dy, c, s, b, False, 64, bits)), (dy, c, s, b)
 
 
 def run_kernels(args):
@@ -432,7 +433,7 @@ def run_kernels(args):
     common = {"n_gpus": 1, "steps": K, "warmup": W, "higher_is_better": True,
               "vs_baseline": None, "data": "synthetic"}
     if args.workload == "qmm":
-        fn, _ = _qmm_case(args.m, args.n, args.k, args.direction, dev)
+        fn, _ = _qmm_case(args.m, args.n, args.k, args.direction, dev, bits=args.bits)
         ms = _time_kernel(fn, K, W, flush)
         tf = 2.0 * args.m * args.n * args.k / (ms / 1000.0) / 1e12
         print(json.dumps({"metric": "int4 quantized_matmul TFLOP/s", "value": tf,
@@ -440,6 +441,7 @@ def run_kernels(args):
                           "dtype": "bf16", **common,
                           "config": {"workload": f"quantized_matmul {args.direction}",
                                      "m": args.m, "w_rows": args.n, "w_cols": args.k,
+                                     "bits": args.bits, "group_size": 64,
                                      "l2": "flushed before every launch"},
                           "roofline": {"bound": "tensor", "achieved": tf, "peak": burst,
                                        "unit": "TFLOP/s", "frac": tf / burst,

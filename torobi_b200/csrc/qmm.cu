@@ -26,16 +26,19 @@
 // the main loop, so base + adapter leave TMEM with one rounding to bf16.
 #include <cuda_bf16.h>
 
+#include <cstdlib>
+
 #include "tq_ptx.cuh"
 #include "tq_runtime.h"
 
 namespace tq {
 namespace {
 
-constexpr int kBM = 128;        // weight-side rows per CTA (UMMA M)
+constexpr int kBM = 128;        // weight-side rows per tile (UMMA M)
 constexpr int kBK = 64;         // reduction elements per pipeline stage
-constexpr int kThreads = 192;   // 6 warps
+constexpr int kThreads = 320;   // 10 warps
 constexpr int kSmemLimit = 232448;
+constexpr int kRing = 4;        // scale/bias prefetch ring (k-steps)
 
 template <int BITS, bool TRANS, int BN>
 struct Cfg {
@@ -48,11 +51,13 @@ struct Cfg {
   static constexpr int LORA_BYTES = ((LUP_BYTES + LDN_BYTES + 1023) / 1024) * 1024;
   static constexpr int BAR_BYTES = 256;
   static constexpr int STAGES_RAW = (kSmemLimit - 1024 - LORA_BYTES - BAR_BYTES) / STAGE_BYTES;
-  static constexpr int STAGES = STAGES_RAW > 6 ? 6 : STAGES_RAW;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr int SMEM = 1024 + LORA_BYTES + STAGES * STAGE_BYTES + BAR_BYTES;
-  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+  static constexpr int ACC_COLS = BN < 32 ? 32 : BN;        // one accumulator
+  static constexpr int TMEM_COLS = 2 * ACC_COLS;            // double-buffered
   static_assert(STAGES >= 2, "shared memory too small for two stages");
   static_assert(SMEM <= kSmemLimit, "shared memory budget");
+  static_assert(3 * 8 * STAGES + 8 * 6 + 8 <= BAR_BYTES, "barrier area");
 };
 
 struct Params {
@@ -67,6 +72,8 @@ struct Params {
   int groups_per_row;        // w_cols / group_size
   int group_shift;
   int lora_rank;             // 0, 8 or 16
+  int tiles_n;               // output tiles along n_out
+  int tiles_total;           // tiles_n * tiles along m
   int* status;
 };
 
@@ -74,6 +81,112 @@ __device__ __forceinline__ uint16_t ldg_u16(const uint16_t* p) {
   return __ldg(reinterpret_cast<const unsigned short*>(p));
 }
 
+// Scale/bias pairs (both bf16 halves equal) one dequantizing thread needs for
+// one k-step: two groups at most (group 32 splits a 64-wide step in two).
+struct GroupPair {
+  uint32_t s0, b0, s1, b1;
+};
+
+template <bool TRANS>
+__device__ __forceinline__ GroupPair load_groups(const Params& p, int t, int out0, int k0) {
+  GroupPair g;
+  const uint32_t gpr = static_cast<uint32_t>(p.groups_per_row);
+  int row;
+  uint32_t g0, g1;
+  bool rv;
+  if constexpr (TRANS) {
+    row = out0 + t;  // weight row = output feature
+    g0 = static_cast<uint32_t>(k0) >> p.group_shift;
+    g1 = static_cast<uint32_t>(k0 + 32) >> p.group_shift;
+    rv = row < p.n_out;
+  } else {
+    const int h = t >> 6;
+    row = k0 + (t & 63);  // weight row = reduction index
+    g0 = static_cast<uint32_t>(out0 + 64 * h) >> p.group_shift;
+    g1 = static_cast<uint32_t>(out0 + 64 * h + 32) >> p.group_shift;
+    rv = row < p.w_rows;
+  }
+  const size_t rb = static_cast<size_t>(row) * gpr;
+  const bool v0 = rv && g0 < gpr, v1 = rv && g1 < gpr;
+  g.s0 = v0 ? bf16_dup(ldg_u16(p.scales + rb + g0)) : 0u;
+  g.b0 = v0 ? bf16_dup(ldg_u16(p.biases + rb + g0)) : 0u;
+  if (g1 == g0) {
+    g.s1 = g.s0;
+    g.b1 = g.b0;
+  } else {
+    g.s1 = v1 ? bf16_dup(ldg_u16(p.scales + rb + g1)) : 0u;
+    g.b1 = v1 ? bf16_dup(ldg_u16(p.biases + rb + g1)) : 0u;
+  }
+  return g;
+}
+
+// Packed codes (shared, as TMA left them) -> bf16 weight tile in the UMMA's
+// 128B-swizzled canonical layout.  t = dequantizing thread (0..127).
+template <int BITS, bool TRANS>
+__device__ __forceinline__ void dequant_tile(uint32_t cb, uint32_t ab, int t, const GroupPair& g) {
+  const uint32_t s2[2] = {g.s0, g.s1};
+  const uint32_t b2[2] = {g.b0, g.b1};
+  if constexpr (TRANS) {
+    // K-major: row r = output feature, 64 k per row (8 chunks of 16 B).
+    const int r = t;
+    if constexpr (BITS == 4) {
+      uint32_t w[8];
+      lds128(cb + swz<32>(r * 32), w[0], w[1], w[2], w[3]);
+      lds128(cb + swz<32>(r * 32 + 16), w[4], w[5], w[6], w[7]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        uint32_t o[4];
+        dequant_u4x8(w[j], s2[j >> 2], b2[j >> 2], o);
+        sts128(ab + r * 128 + ((j ^ (r & 7)) << 4), o[0], o[1], o[2], o[3]);
+      }
+    } else {
+      uint32_t w[16];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        lds128(cb + swz<64>(r * 64 + c * 16), w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        uint32_t o0[2], o1[2];
+        dequant_u8x4(w[2 * j], s2[j >> 2], b2[j >> 2], o0);
+        dequant_u8x4(w[2 * j + 1], s2[j >> 2], b2[j >> 2], o1);
+        sts128(ab + r * 128 + ((j ^ (r & 7)) << 4), o0[0], o0[1], o1[0], o1[1]);
+      }
+    }
+  } else {
+    // MN-major: kr = reduction row (0..63), h = which 64 outputs; atoms of
+    // 64 outputs x 8 reduction rows, 8 K-groups per 64-output block.
+    const int kr = t & 63;
+    const int h = t >> 6;
+    const uint32_t row_off = h * 8192 + (kr >> 3) * 1024 + (kr & 7) * 128;
+    if constexpr (BITS == 4) {
+      uint32_t w[8];
+      lds128(cb + swz<64>(kr * 64 + (2 * h) * 16), w[0], w[1], w[2], w[3]);
+      lds128(cb + swz<64>(kr * 64 + (2 * h + 1) * 16), w[4], w[5], w[6], w[7]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        uint32_t o[4];
+        dequant_u4x8(w[j], s2[j >> 2], b2[j >> 2], o);
+        sts128(ab + row_off + ((j ^ (kr & 7)) << 4), o[0], o[1], o[2], o[3]);
+      }
+    } else {
+      uint32_t w[16];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        lds128(cb + swz<128>(kr * 128 + (4 * h + c) * 16), w[4 * c], w[4 * c + 1], w[4 * c + 2],
+               w[4 * c + 3]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        uint32_t o0[2], o1[2];
+        dequant_u8x4(w[2 * j], s2[j >> 2], b2[j >> 2], o0);
+        dequant_u8x4(w[2 * j + 1], s2[j >> 2], b2[j >> 2], o1);
+        sts128(ab + row_off + ((j ^ (kr & 7)) << 4), o0[0], o0[1], o1[0], o1[1]);
+      }
+    }
+  }
+}
+
+// Persistent: CTA b takes tiles b, b + grid, ...; tile t covers output
+// features (t % tiles_n) * 128 and tokens (t / tiles_n) * BN.
 template <int BITS, bool TRANS, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     qmm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_c,
@@ -96,21 +209,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto full_b = [&](int s) { return bars + 8u * s; };
   auto wready_b = [&](int s) { return bars + 8u * (S + s); };
   auto empty_b = [&](int s) { return bars + 8u * (2 * S + s); };
-  const uint32_t lora_b = bars + 8u * (3 * S);
-  const uint32_t acc_b = bars + 8u * (3 * S + 1);
-  const uint32_t tmem_slot = bars + 8u * (3 * S + 2);
+  const uint32_t lora_full = bars + 8u * (3 * S);
+  const uint32_t lora_empty = bars + 8u * (3 * S + 1);
+  auto acc_full = [&](int b) { return bars + 8u * (3 * S + 2 + b); };
+  auto acc_empty = [&](int b) { return bars + 8u * (3 * S + 4 + b); };
+  const uint32_t tmem_slot = bars + 8u * (3 * S + 6);
   volatile uint32_t* tmem_slot_ptr =
       reinterpret_cast<volatile uint32_t*>(gbase + (tmem_slot - base));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int out0 = blockIdx.x * kBM;
-  const int m0 = blockIdx.y * BN;
   const int num_k = (p.k_red + kBK - 1) / kBK;
   const bool has_lora = p.lora_rank > 0;
   const int lora_chunks = p.lora_rank / 8;
+  const int my_tiles = static_cast<int>(blockIdx.x) < p.tiles_total
+                           ? (p.tiles_total - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1
+                           : 0;
+  auto tile_out0 = [&](int lt) { return ((blockIdx.x + lt * gridDim.x) % p.tiles_n) * kBM; };
+  auto tile_m0 = [&](int lt) { return ((blockIdx.x + lt * gridDim.x) / p.tiles_n) * BN; };
 
-  // Zero the LoRA tiles: with rank 8 the second K-chunk stays zero.
+  // Zero the LoRA tiles once: with rank 8 the second K-chunk stays zero.
   if (has_lora) {
     for (int i = threadIdx.x; i < C::LORA_BYTES / 16; i += kThreads)
       sts128(base + 16u * i, 0u, 0u, 0u, 0u);
@@ -122,8 +240,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(wready_b(s), 4);
       mbar_init(empty_b(s), 1);
     }
-    mbar_init(lora_b, 1);
-    mbar_init(acc_b, 1);
+    mbar_init(lora_full, 1);
+    mbar_init(lora_empty, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full(b), 1);
+      mbar_init(acc_empty(b), 4);
+    }
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -143,204 +265,173 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (has_lora) {
         tma_prefetch_desc(&tm_lup);
         tma_prefetch_desc(&tm_ldn);
-        const uint32_t bytes = lora_chunks * (kBM * 16 + BN * 16);
-        mbar_arrive_expect_tx(lora_b, bytes);
-        for (int ch = 0; ch < lora_chunks; ++ch) {
-          if constexpr (TRANS) {
-            // B [n_out, rank]: K-major, no swizzle; chunk = 8 rank columns.
-            tma_load_2d(lup + ch * kBM * 16, &tm_lup, lora_b, ch * 8, out0);
-          } else {
-            // A [rank, k]: MN-major 128B-swizzled atoms (64 k x 8 rank).
-            tma_load_2d(lup + ch * 1024, &tm_lup, lora_b, out0, ch * 8);
-            tma_load_2d(lup + 2048 + ch * 1024, &tm_lup, lora_b, out0 + 64, ch * 8);
-          }
-          tma_load_2d(ldn + ch * BN * 16, &tm_ldn, lora_b, ch * 8, m0);
-        }
       }
       bool ok = true;
-      int issued = 0;
-      for (int i = 0; i < num_k && ok; ++i) {
-        const int s = i % S;
-        const uint32_t ph = (i / S) & 1;
-        ok = mbar_wait(empty_b(s), ph ^ 1, p.status);
-        if (!ok) break;
-        mbar_arrive_expect_tx(full_b(s), C::X_BYTES + C::C_BYTES);
-        tma_load_2d(x_s(s), &tm_x, full_b(s), i * kBK, m0);
-        if constexpr (TRANS)
-          tma_load_2d(c_s(s), &tm_c, full_b(s), i * kBK * BITS / 32, out0);
-        else
-          tma_load_2d(c_s(s), &tm_c, full_b(s), out0 * BITS / 32, i * kBK);
-        ++issued;
+      int it = 0;
+      int lora_loads = 0;
+      for (int lt = 0; lt < my_tiles && ok; ++lt) {
+        const int out0 = tile_out0(lt), m0 = tile_m0(lt);
+        if (has_lora) {
+          ok = mbar_wait(lora_empty, (lt & 1) ^ 1, p.status);
+          if (!ok) break;
+          mbar_arrive_expect_tx(lora_full, lora_chunks * (kBM * 16 + BN * 16));
+          for (int ch = 0; ch < lora_chunks; ++ch) {
+            if constexpr (TRANS) {
+              // B [n_out, rank]: K-major, no swizzle; chunk = 8 rank columns.
+              tma_load_2d(lup + ch * kBM * 16, &tm_lup, lora_full, ch * 8, out0);
+            } else {
+              // A [rank, k]: MN-major 128B-swizzled atoms (64 k x 8 rank).
+              tma_load_2d(lup + ch * 1024, &tm_lup, lora_full, out0, ch * 8);
+              tma_load_2d(lup + 2048 + ch * 1024, &tm_lup, lora_full, out0 + 64, ch * 8);
+            }
+            tma_load_2d(ldn + ch * BN * 16, &tm_ldn, lora_full, ch * 8, m0);
+          }
+          ++lora_loads;
+        }
+        for (int kk = 0; kk < num_k; ++kk, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          ok = mbar_wait(empty_b(s), ph ^ 1, p.status);
+          if (!ok) break;
+          mbar_arrive_expect_tx(full_b(s), C::X_BYTES + C::C_BYTES);
+          tma_load_2d(x_s(s), &tm_x, full_b(s), kk * kBK, m0);
+          if constexpr (TRANS)
+            tma_load_2d(c_s(s), &tm_c, full_b(s), kk * kBK * BITS / 32, out0);
+          else
+            tma_load_2d(c_s(s), &tm_c, full_b(s), out0 * BITS / 32, kk * kBK);
+        }
       }
       // Never leave a copy in flight: wait for the last phase of every stage.
-      for (int i = issued - S < 0 ? 0 : issued - S; i < issued; ++i)
+      for (int i = it - S < 0 ? 0 : it - S; i < it; ++i)
         mbar_wait(full_b(i % S), (i / S) & 1, p.status);
-      if (has_lora) mbar_wait(lora_b, 0, p.status);
+      if (lora_loads > 0) mbar_wait(lora_full, (lora_loads - 1) & 1, p.status);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
     if (elect_one_sync()) {
       constexpr uint32_t idesc = make_idesc_bf16(kBM, BN, !TRANS, false);
-      uint32_t acc = 0;
       bool ok = true;
-      if (has_lora) {
-        ok = mbar_wait(lora_b, 0, p.status);
-        tc_fence_after();
-        uint64_t adesc;
-        if constexpr (TRANS)
-          adesc = make_sdesc(lup, kBM * 16, 128, kSwNone);  // LBO: K chunk, SBO: 8-row group
-        else
-          adesc = make_sdesc(lup, 2048, 1024, kSw128);     // LBO: MN atom, SBO: K group
-        const uint64_t bdesc = make_sdesc(ldn, BN * 16, 128, kSwNone);
-        if (ok) {
-          umma_bf16(tmem, adesc, bdesc, idesc, 0);
-          acc = 1;
-        }
-      }
-      for (int i = 0; i < num_k && ok; ++i) {
-        const int s = i % S;
-        const uint32_t ph = (i / S) & 1;
-        ok = mbar_wait(full_b(s), ph, p.status) && mbar_wait(wready_b(s), ph, p.status);
+      int it = 0;
+      for (int lt = 0; lt < my_tiles && ok; ++lt) {
+        const int buf = lt & 1;
+        ok = mbar_wait(acc_empty(buf), ((lt >> 1) & 1) ^ 1, p.status);
         if (!ok) break;
         tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk) {
+        const uint32_t d = tmem + buf * C::ACC_COLS;
+        uint32_t acc = 0;
+        if (has_lora) {
+          ok = mbar_wait(lora_full, lt & 1, p.status);
+          if (!ok) break;
+          tc_fence_after();
           uint64_t adesc;
           if constexpr (TRANS)
-            adesc = make_sdesc(a_s(s) + kk * 32, 16, 1024, kSw128);
+            adesc = make_sdesc(lup, kBM * 16, 128, kSwNone);  // LBO: K chunk, SBO: 8-row group
           else
-            adesc = make_sdesc(a_s(s) + kk * 2048, 8192, 1024, kSw128);
-          const uint64_t bdesc = make_sdesc(x_s(s) + kk * 32, 16, 1024, kSw128);
-          umma_bf16(tmem, adesc, bdesc, idesc, acc);
+            adesc = make_sdesc(lup, 2048, 1024, kSw128);     // LBO: MN atom, SBO: K group
+          const uint64_t bdesc = make_sdesc(ldn, BN * 16, 128, kSwNone);
+          umma_bf16(d, adesc, bdesc, idesc, 0);
+          umma_commit(lora_empty);
           acc = 1;
         }
-        umma_commit(empty_b(s));
+        for (int kk = 0; kk < num_k; ++kk, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          ok = mbar_wait(full_b(s), ph, p.status) && mbar_wait(wready_b(s), ph, p.status);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int k4 = 0; k4 < kBK / 16; ++k4) {
+            uint64_t adesc;
+            if constexpr (TRANS)
+              adesc = make_sdesc(a_s(s) + k4 * 32, 16, 1024, kSw128);
+            else
+              adesc = make_sdesc(a_s(s) + k4 * 2048, 8192, 1024, kSw128);
+            const uint64_t bdesc = make_sdesc(x_s(s) + k4 * 32, 16, 1024, kSw128);
+            umma_bf16(d, adesc, bdesc, idesc, acc);
+            acc = 1;
+          }
+          umma_commit(empty_b(s));
+        }
+        umma_commit(acc_full(buf));
       }
-      umma_commit(acc_b);
-      mbar_wait(acc_b, 0, p.status);  // nothing may outlive the CTA's TMEM
+      // Nothing may outlive the CTA's TMEM: the last commit covers every UMMA.
+      if (my_tiles > 0)
+        mbar_wait(acc_full((my_tiles - 1) & 1), ((my_tiles - 1) >> 1) & 1, p.status);
     }
-  } else {
+  } else if (warp < 6) {
     // ---------------------------------------------------- dequant warps
     const int t = threadIdx.x - 64;  // 0..127
-    const uint32_t gpr = static_cast<uint32_t>(p.groups_per_row);
-    bool ok = true;
-    for (int i = 0; i < num_k && ok; ++i) {
-      const int s = i % S;
-      const uint32_t ph = (i / S) & 1;
-      const int k0 = i * kBK;
-      // Scale/bias for this thread's elements (two groups at most).
-      uint32_t s2[2], b2[2];
-      if constexpr (TRANS) {
-        const int row = out0 + t;  // weight row
-        const uint32_t g0 = static_cast<uint32_t>(k0) >> p.group_shift;
-        const uint32_t g1 = static_cast<uint32_t>(k0 + 32) >> p.group_shift;
-        const bool rv = row < p.n_out;
-        const size_t rb = static_cast<size_t>(row) * gpr;
-        s2[0] = (rv && g0 < gpr) ? bf16_dup(ldg_u16(p.scales + rb + g0)) : 0u;
-        b2[0] = (rv && g0 < gpr) ? bf16_dup(ldg_u16(p.biases + rb + g0)) : 0u;
-        s2[1] = (rv && g1 < gpr) ? bf16_dup(ldg_u16(p.scales + rb + g1)) : 0u;
-        b2[1] = (rv && g1 < gpr) ? bf16_dup(ldg_u16(p.biases + rb + g1)) : 0u;
-      } else {
-        const int kr = t & 63;
-        const int h = t >> 6;
-        const int row = k0 + kr;  // weight row (reduction index)
-        const uint32_t g0 = static_cast<uint32_t>(out0 + 64 * h) >> p.group_shift;
-        const uint32_t g1 = static_cast<uint32_t>(out0 + 64 * h + 32) >> p.group_shift;
-        const bool rv = row < p.w_rows;
-        const size_t rb = static_cast<size_t>(row) * gpr;
-        s2[0] = (rv && g0 < gpr) ? bf16_dup(ldg_u16(p.scales + rb + g0)) : 0u;
-        b2[0] = (rv && g0 < gpr) ? bf16_dup(ldg_u16(p.biases + rb + g0)) : 0u;
-        s2[1] = (rv && g1 < gpr) ? bf16_dup(ldg_u16(p.scales + rb + g1)) : 0u;
-        b2[1] = (rv && g1 < gpr) ? bf16_dup(ldg_u16(p.biases + rb + g1)) : 0u;
+    const int total = my_tiles * num_k;
+    GroupPair ring[kRing];
+    auto coords = [&](int j, int& out0, int& k0) {
+      const int lt = j / num_k;
+      out0 = tile_out0(lt);
+      k0 = (j - lt * num_k) * kBK;
+    };
+#pragma unroll
+    for (int u = 0; u < kRing - 1; ++u) {
+      if (u < total) {
+        int out0, k0;
+        coords(u, out0, k0);
+        ring[u] = load_groups<TRANS>(p, t, out0, k0);
       }
-      ok = mbar_wait(full_b(s), ph, p.status);
-      if (!ok) break;
-      const uint32_t cb = c_s(s);
-      const uint32_t ab = a_s(s);
-      if constexpr (TRANS) {
-        const int r = t;
-        if constexpr (BITS == 4) {
-          uint32_t w[8];
-          lds128(cb + swz<32>(r * 32), w[0], w[1], w[2], w[3]);
-          lds128(cb + swz<32>(r * 32 + 16), w[4], w[5], w[6], w[7]);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            uint32_t o[4];
-            dequant_u4x8(w[j], s2[j >> 2], b2[j >> 2], o);
-            sts128(ab + r * 128 + ((j ^ (r & 7)) << 4), o[0], o[1], o[2], o[3]);
-          }
-        } else {
-          uint32_t w[16];
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            lds128(cb + swz<64>(r * 64 + c * 16), w[4 * c], w[4 * c + 1], w[4 * c + 2],
-                   w[4 * c + 3]);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            uint32_t o0[2], o1[2];
-            dequant_u8x4(w[2 * j], s2[j >> 2], b2[j >> 2], o0);
-            dequant_u8x4(w[2 * j + 1], s2[j >> 2], b2[j >> 2], o1);
-            sts128(ab + r * 128 + ((j ^ (r & 7)) << 4), o0[0], o0[1], o1[0], o1[1]);
-          }
-        }
-      } else {
-        const int kr = t & 63;
-        const int h = t >> 6;
-        const uint32_t row_off = h * 8192 + (kr >> 3) * 1024 + (kr & 7) * 128;
-        if constexpr (BITS == 4) {
-          uint32_t w[8];
-          lds128(cb + swz<64>(kr * 64 + (2 * h) * 16), w[0], w[1], w[2], w[3]);
-          lds128(cb + swz<64>(kr * 64 + (2 * h + 1) * 16), w[4], w[5], w[6], w[7]);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            uint32_t o[4];
-            dequant_u4x8(w[j], s2[j >> 2], b2[j >> 2], o);
-            sts128(ab + row_off + ((j ^ (kr & 7)) << 4), o[0], o[1], o[2], o[3]);
-          }
-        } else {
-          uint32_t w[16];
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            lds128(cb + swz<128>(kr * 128 + (4 * h + c) * 16), w[4 * c], w[4 * c + 1],
-                   w[4 * c + 2], w[4 * c + 3]);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            uint32_t o0[2], o1[2];
-            dequant_u8x4(w[2 * j], s2[j >> 2], b2[j >> 2], o0);
-            dequant_u8x4(w[2 * j + 1], s2[j >> 2], b2[j >> 2], o1);
-            sts128(ab + row_off + ((j ^ (kr & 7)) << 4), o0[0], o0[1], o1[0], o1[1]);
-          }
-        }
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(wready_b(s));
     }
-
+    bool ok = true;
+    for (int j0 = 0; j0 < total && ok; j0 += kRing) {
+#pragma unroll
+      for (int u = 0; u < kRing; ++u) {
+        const int j = j0 + u;
+        if (j < total && ok) {
+          if (j + kRing - 1 < total) {
+            int out0, k0;
+            coords(j + kRing - 1, out0, k0);
+            ring[(u + kRing - 1) % kRing] = load_groups<TRANS>(p, t, out0, k0);
+          }
+          const int s = j % S;
+          ok = mbar_wait(full_b(s), (j / S) & 1, p.status);
+          if (ok) {
+            dequant_tile<BITS, TRANS>(c_s(s), a_s(s), t, ring[u]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(wready_b(s));
+          }
+        }
+      }
+    }
+  } else {
     // ------------------------------------------------------------ epilogue
-    ok = mbar_wait(acc_b, 0, p.status) && ok;
-    tc_fence_after();
     const int q = warp & 3;              // TMEM lane quadrant this warp may read
     const int r = q * 32 + lane;         // output feature within the tile
-    const int og = out0 + r;
-    float bias = 0.0f;
-    if (p.bias_vec && og < p.n_out) bias = __uint_as_float(uint32_t(ldg_u16(p.bias_vec + og)) << 16);
+    bool ok = true;
+    for (int lt = 0; lt < my_tiles && ok; ++lt) {
+      const int buf = lt & 1;
+      ok = mbar_wait(acc_full(buf), (lt >> 1) & 1, p.status);
+      tc_fence_after();
+      const int out0 = tile_out0(lt), m0 = tile_m0(lt);
+      const int og = out0 + r;
+      float bias = 0.0f;
+      if (p.bias_vec && og < p.n_out)
+        bias = __uint_as_float(uint32_t(ldg_u16(p.bias_vec + og)) << 16);
+      const uint32_t d = tmem + buf * C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16);
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, v);
-      tmem_ld_wait();
-      if (og < p.n_out) {
-        const int mlim = p.m - (m0 + c0);
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(d + c0, v);
+        tmem_ld_wait();
+        if (ok && og < p.n_out) {
+          const int mlim = p.m - (m0 + c0);
+          uint16_t* yp = p.y + static_cast<size_t>(m0 + c0) * p.n_out + og;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          if (j < mlim) {
-            const float f = __uint_as_float(v[j]) + bias;
-            p.y[static_cast<size_t>(m0 + c0 + j) * p.n_out + og] =
-                __bfloat16_as_ushort(__float2bfloat16_rn(f));
+          for (int j = 0; j < 32; ++j) {
+            if (j < mlim)
+              yp[static_cast<size_t>(j) * p.n_out] =
+                  __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[j]) + bias));
           }
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty(buf));
     }
   }
 
@@ -437,13 +528,15 @@ int launch(const Args& a, cudaStream_t stream, int* status) {
   p.groups_per_row = static_cast<int>(a.w_cols / a.group_size);
   p.group_shift = a.group_size == 32 ? 5 : (a.group_size == 64 ? 6 : 7);
   p.lora_rank = a.rank;
+  p.tiles_n = static_cast<int>((n_out + kBM - 1) / kBM);
+  const int64_t tiles_m = (a.m + BN - 1) / BN;
+  p.tiles_total = static_cast<int>(p.tiles_n * tiles_m);
   p.status = status;
   auto kernel = qmm_kernel<BITS, TRANS, BN>;
   rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
                   "cudaFuncSetAttribute(qmm smem)");
   if (rc) return rc;
-  const dim3 grid(static_cast<unsigned>((n_out + kBM - 1) / kBM),
-                  static_cast<unsigned>((a.m + BN - 1) / BN));
+  const int grid = p.tiles_total < sm_count() ? p.tiles_total : sm_count();
   kernel<<<grid, kThreads, C::SMEM, stream>>>(tm_x, tm_c, tm_lup, tm_ldn, p);
   return check_cuda(cudaGetLastError(), "qmm launch");
 }
@@ -456,6 +549,14 @@ int launch_bn(const Args& a, cudaStream_t stream, int* status) {
   // Largest token tile that still gives every SM a CTA (M-side padding is
   // zero-filled by TMA and never stored).
   int bn = 32;
+  // TQ_QMM_BN pins the token tile (256, 128, 64 or 32) for tuning runs.
+  static const int forced = [] {
+    const char* e = getenv("TQ_QMM_BN");
+    return e ? atoi(e) : 0;
+  }();
+  if (forced == 256 || forced == 128 || forced == 64 || forced == 32) {
+    bn = forced;
+  } else {
   for (int cand : {256, 128, 64}) {
     if (a.m >= cand / 2 && ((a.m + cand - 1) / cand) * tiles_n >= sms) {
       bn = cand;
@@ -463,6 +564,7 @@ int launch_bn(const Args& a, cudaStream_t stream, int* status) {
     }
   }
   if (bn == 32 && a.m > 32) bn = a.m > 128 ? 128 : 64;
+  }
   switch (bn) {
     case 256: return launch<BITS, TRANS, 256>(a, stream, status);
     case 128: return launch<BITS, TRANS, 128>(a, stream, status);
