@@ -47,6 +47,9 @@ CASES = [
     (200, 264, 384, 16, 32.0, 4, 32, False),
     (130, 512, 256, 16, 32.0, 8, 128, True),
     (64, 128, 128, 8, 8.0, 8, 64, False),
+    # scale tiles staged by TMA (groups per row a multiple of 8)
+    (300, 520, 1024, 16, 32.0, 4, 64, True),
+    (96, 1024, 2048, 8, 16.0, 8, 32, False),
 ]
 
 

@@ -25,6 +25,10 @@ CASES = [
     (257, 128, 128, 4, 128),
     (129, 392, 640, 4, 32),
     (640, 256, 1024, 8, 64),
+    # scale rows 16-byte aligned (groups per row % 8 == 0): scale tiles by TMA
+    (257, 392, 1024, 4, 32),
+    (1000, 1032, 2048, 4, 128),
+    (33, 264, 4096, 8, 64),
 ]
 
 

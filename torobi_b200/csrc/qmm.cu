@@ -1,19 +1,22 @@
 // quantized_matmul on the 5th-generation tensor cores (tcgen05 / TMEM), with
 // the LoRA up-projection and the linear's bias fused into the accumulator.
 //
-// One CTA computes a 128 x BN tile of the output TRANSPOSED in tensor memory:
+// Each CTA (one per SM, persistent) computes 128 x BN tiles of the output
+// TRANSPOSED in tensor memory:
 // the UMMA's M side (128 TMEM lanes) is the weight's output features and its
 // N side (BN columns) is the tokens.  Putting the quantized weight on the M
 // side halves the dequantization work per MMA flop against the other
 // orientation (a 128-row weight tile feeds a 128 x BN MMA instead of a BN-row
 // tile feeding a BN x 128 one).
 //
-//   warp 0      TMA producer: activation tile (bf16, 128B swizzle) and the raw
-//               packed-code tile of each stage; the LoRA tiles once.
+//   warp 0      TMA producer: activation tile (bf16, 128B swizzle), the raw
+//               packed-code tile and the group scale/bias tiles of each stage;
+//               the LoRA tiles once per output tile.
 //   warp 1      TMEM allocator and the single UMMA-issuing thread.
 //   warps 2-5   dequantizers: packed codes (shared) -> bf16 weight tile in the
-//               UMMA canonical 128B-swizzled layout, w = RNE(scale*q + bias);
-//               afterwards the epilogue (TMEM -> registers -> bf16 -> global).
+//               UMMA canonical 128B-swizzled layout, w = RNE(scale*q + bias).
+//   warps 6-9   epilogue: TMEM -> registers -> (+ bias) -> bf16 -> global,
+//               overlapped with the next tile (two TMEM accumulators).
 //
 // transpose (linear forward, y = x . W^T): the reduction runs along W's packed
 // axis, so the dequantized tile is K-major.  Backward wrt x (y = dy . W): the
@@ -38,26 +41,41 @@ constexpr int kBM = 128;        // weight-side rows per tile (UMMA M)
 constexpr int kBK = 64;         // reduction elements per pipeline stage
 constexpr int kThreads = 320;   // 10 warps
 constexpr int kSmemLimit = 232448;
-constexpr int kRing = 4;        // scale/bias prefetch ring (k-steps)
+constexpr int kRing = 4;        // fallback path: scale/bias register ring (k-steps)
 
-template <int BITS, bool TRANS, int BN>
+// Shared-memory plan.  Two rings:
+//   stage ring (S deep, filled by TMA): activation tile, packed codes and --
+//     when the scale rows are 16-byte aligned (STMA) -- the group scale and
+//     bias tiles the step needs;
+//   dequantized-weight ring (A deep, written by the dequantizing warps).
+// Splitting them lets the TMA run S stages ahead while only A bf16 weight
+// tiles are held.
+template <int BITS, bool TRANS, int BN, bool STMA>
 struct Cfg {
   static constexpr int X_BYTES = BN * kBK * 2;
   static constexpr int A_BYTES = kBM * kBK * 2;
   static constexpr int C_BYTES = kBM * kBK * BITS / 8;
-  static constexpr int STAGE_BYTES = X_BYTES + A_BYTES + C_BYTES;
+  // Scale (and bias) tile: 8 groups (16 bytes, the TMA minimum) x the rows
+  // the step touches: 128 output features forward, 64 weight rows backward.
+  static constexpr int SC_ROWS = TRANS ? kBM : kBK;
+  static constexpr int SC_BYTES = STMA ? SC_ROWS * 16 : 0;
+  static constexpr int STAGE_BYTES = X_BYTES + C_BYTES + 2 * SC_BYTES;
   static constexpr int LUP_BYTES = kBM * 16 * 2;            // [128 x 16] bf16
   static constexpr int LDN_BYTES = BN * 16 * 2;             // [BN x 16] bf16
   static constexpr int LORA_BYTES = ((LUP_BYTES + LDN_BYTES + 1023) / 1024) * 1024;
   static constexpr int BAR_BYTES = 256;
-  static constexpr int STAGES_RAW = (kSmemLimit - 1024 - LORA_BYTES - BAR_BYTES) / STAGE_BYTES;
+  static constexpr int FIXED = 1024 + LORA_BYTES + BAR_BYTES;
+  static constexpr int S3 = (kSmemLimit - FIXED - 3 * A_BYTES) / STAGE_BYTES;
+  static constexpr int A_BUFS = S3 >= 4 ? 3 : 2;
+  static constexpr int STAGES_RAW = (kSmemLimit - FIXED - A_BUFS * A_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
-  static constexpr int SMEM = 1024 + LORA_BYTES + STAGES * STAGE_BYTES + BAR_BYTES;
+  static constexpr int SMEM = FIXED + A_BUFS * A_BYTES + STAGES * STAGE_BYTES;
   static constexpr int ACC_COLS = BN < 32 ? 32 : BN;        // one accumulator
   static constexpr int TMEM_COLS = 2 * ACC_COLS;            // double-buffered
   static_assert(STAGES >= 2, "shared memory too small for two stages");
   static_assert(SMEM <= kSmemLimit, "shared memory budget");
-  static_assert(3 * 8 * STAGES + 8 * 6 + 8 <= BAR_BYTES, "barrier area");
+  static_assert(8 * (2 * STAGES + 2 * A_BUFS + 6) + 8 <= BAR_BYTES, "barrier area");
+  static_assert(STAGE_BYTES % 1024 == 0, "stage tiles stay 1024-byte aligned");
 };
 
 struct Params {
@@ -81,51 +99,76 @@ __device__ __forceinline__ uint16_t ldg_u16(const uint16_t* p) {
   return __ldg(reinterpret_cast<const unsigned short*>(p));
 }
 
-// Scale/bias pairs (both bf16 halves equal) one dequantizing thread needs for
-// one k-step: two groups at most (group 32 splits a 64-wide step in two).
-struct GroupPair {
+__device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// Groups of one k-step for dequantizing thread t (0..127): first and second
+// (group 32 splits a 64-wide step in two), and the weight row they sit on.
+struct GroupCoord {
+  int row;       // weight row
+  uint32_t g0, g1;
+  bool rv;       // row inside the weight
+};
+
+template <bool TRANS>
+__device__ __forceinline__ GroupCoord group_coord(const Params& p, int t, int out0, int k0) {
+  GroupCoord c;
+  if constexpr (TRANS) {
+    c.row = out0 + t;  // weight row = output feature
+    c.g0 = static_cast<uint32_t>(k0) >> p.group_shift;
+    c.g1 = static_cast<uint32_t>(k0 + 32) >> p.group_shift;
+    c.rv = c.row < p.n_out;
+  } else {
+    const int h = t >> 6;
+    c.row = k0 + (t & 63);  // weight row = reduction index
+    c.g0 = static_cast<uint32_t>(out0 + 64 * h) >> p.group_shift;
+    c.g1 = static_cast<uint32_t>(out0 + 64 * h + 32) >> p.group_shift;
+    c.rv = c.row < p.w_rows;
+  }
+  return c;
+}
+
+// First group of the 8-group window a step's TMA scale tile covers (x of the
+// box, a multiple of 8 so the copy starts on a 16-byte boundary).
+template <bool TRANS>
+__device__ __forceinline__ int scale_window(const Params& p, int out0, int k0) {
+  return static_cast<int>((static_cast<uint32_t>(TRANS ? k0 : out0) >> p.group_shift) & ~7u);
+}
+
+// Fallback path (scale rows not 16-byte aligned): raw bits loaded by the
+// dequantizing thread kRing-1 steps ahead; bit 16 flags out-of-range.
+struct GroupRaw {
   uint32_t s0, b0, s1, b1;
 };
 
 template <bool TRANS>
-__device__ __forceinline__ GroupPair load_groups(const Params& p, int t, int out0, int k0) {
-  GroupPair g;
+__device__ __forceinline__ GroupRaw load_groups(const Params& p, int t, int out0, int k0) {
+  const GroupCoord c = group_coord<TRANS>(p, t, out0, k0);
   const uint32_t gpr = static_cast<uint32_t>(p.groups_per_row);
-  int row;
-  uint32_t g0, g1;
-  bool rv;
-  if constexpr (TRANS) {
-    row = out0 + t;  // weight row = output feature
-    g0 = static_cast<uint32_t>(k0) >> p.group_shift;
-    g1 = static_cast<uint32_t>(k0 + 32) >> p.group_shift;
-    rv = row < p.n_out;
-  } else {
-    const int h = t >> 6;
-    row = k0 + (t & 63);  // weight row = reduction index
-    g0 = static_cast<uint32_t>(out0 + 64 * h) >> p.group_shift;
-    g1 = static_cast<uint32_t>(out0 + 64 * h + 32) >> p.group_shift;
-    rv = row < p.w_rows;
-  }
-  const size_t rb = static_cast<size_t>(row) * gpr;
-  const bool v0 = rv && g0 < gpr, v1 = rv && g1 < gpr;
-  g.s0 = v0 ? bf16_dup(ldg_u16(p.scales + rb + g0)) : 0u;
-  g.b0 = v0 ? bf16_dup(ldg_u16(p.biases + rb + g0)) : 0u;
-  if (g1 == g0) {
-    g.s1 = g.s0;
-    g.b1 = g.b0;
-  } else {
-    g.s1 = v1 ? bf16_dup(ldg_u16(p.scales + rb + g1)) : 0u;
-    g.b1 = v1 ? bf16_dup(ldg_u16(p.biases + rb + g1)) : 0u;
-  }
+  const size_t rb = static_cast<size_t>(c.row) * gpr;
+  const bool v0 = c.rv && c.g0 < gpr, v1 = c.rv && c.g1 < gpr;
+  const size_t i0 = v0 ? rb + c.g0 : 0, i1 = v1 ? rb + c.g1 : 0;
+  GroupRaw g;
+  g.s0 = ldg_u16(p.scales + i0) | (v0 ? 0u : 0x10000u);
+  g.b0 = ldg_u16(p.biases + i0);
+  g.s1 = ldg_u16(p.scales + i1) | (v1 ? 0u : 0x10000u);
+  g.b1 = ldg_u16(p.biases + i1);
   return g;
 }
 
+__device__ __forceinline__ uint32_t widen(uint32_t raw, uint32_t flag_from) {
+  return (flag_from & 0x10000u) ? 0u : bf16_dup(static_cast<uint16_t>(raw));
+}
+
 // Packed codes (shared, as TMA left them) -> bf16 weight tile in the UMMA's
-// 128B-swizzled canonical layout.  t = dequantizing thread (0..127).
+// 128B-swizzled canonical layout.  t = dequantizing thread (0..127); s2/b2
+// the bf16 scale/bias pairs of its first and second group.
 template <int BITS, bool TRANS>
-__device__ __forceinline__ void dequant_tile(uint32_t cb, uint32_t ab, int t, const GroupPair& g) {
-  const uint32_t s2[2] = {g.s0, g.s1};
-  const uint32_t b2[2] = {g.b0, g.b1};
+__device__ __forceinline__ void dequant_tile(uint32_t cb, uint32_t ab, int t, const uint32_t (&s2)[2],
+                                             const uint32_t (&b2)[2]) {
   if constexpr (TRANS) {
     // K-major: row r = output feature, 64 k per row (8 chunks of 16 B).
     const int r = t;
@@ -187,13 +230,15 @@ __device__ __forceinline__ void dequant_tile(uint32_t cb, uint32_t ab, int t, co
 
 // Persistent: CTA b takes tiles b, b + grid, ...; tile t covers output
 // features (t % tiles_n) * 128 and tokens (t / tiles_n) * BN.
-template <int BITS, bool TRANS, int BN>
+template <int BITS, bool TRANS, int BN, bool STMA>
 __global__ void __launch_bounds__(kThreads, 1)
     qmm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_c,
-               const __grid_constant__ CUtensorMap tm_lup,
-               const __grid_constant__ CUtensorMap tm_ldn, const Params p) {
-  using C = Cfg<BITS, TRANS, BN>;
+               const __grid_constant__ CUtensorMap tm_lup, const __grid_constant__ CUtensorMap tm_ldn,
+               const __grid_constant__ CUtensorMap tm_sc, const __grid_constant__ CUtensorMap tm_bi,
+               const Params p) {
+  using C = Cfg<BITS, TRANS, BN, STMA>;
   constexpr int S = C::STAGES;
+  constexpr int A = C::A_BUFS;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -201,19 +246,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const uint32_t lup = base;                                  // LoRA up tile
   const uint32_t ldn = base + C::LUP_BYTES;                   // LoRA down tile
-  const uint32_t stages = base + C::LORA_BYTES;
+  const uint32_t abufs = base + C::LORA_BYTES;                // dequantized-weight ring
+  const uint32_t stages = abufs + A * C::A_BYTES;             // TMA stage ring
+  auto a_s = [&](int a) { return abufs + a * C::A_BYTES; };
   auto x_s = [&](int s) { return stages + s * C::STAGE_BYTES; };
-  auto a_s = [&](int s) { return stages + s * C::STAGE_BYTES + C::X_BYTES; };
-  auto c_s = [&](int s) { return stages + s * C::STAGE_BYTES + C::X_BYTES + C::A_BYTES; };
+  auto c_s = [&](int s) { return stages + s * C::STAGE_BYTES + C::X_BYTES; };
+  auto sc_s = [&](int s) { return stages + s * C::STAGE_BYTES + C::X_BYTES + C::C_BYTES; };
+  auto bi_s = [&](int s) { return sc_s(s) + C::SC_BYTES; };
   const uint32_t bars = stages + S * C::STAGE_BYTES;
   auto full_b = [&](int s) { return bars + 8u * s; };
-  auto wready_b = [&](int s) { return bars + 8u * (S + s); };
-  auto empty_b = [&](int s) { return bars + 8u * (2 * S + s); };
-  const uint32_t lora_full = bars + 8u * (3 * S);
-  const uint32_t lora_empty = bars + 8u * (3 * S + 1);
-  auto acc_full = [&](int b) { return bars + 8u * (3 * S + 2 + b); };
-  auto acc_empty = [&](int b) { return bars + 8u * (3 * S + 4 + b); };
-  const uint32_t tmem_slot = bars + 8u * (3 * S + 6);
+  auto empty_b = [&](int s) { return bars + 8u * (S + s); };
+  auto aready_b = [&](int a) { return bars + 8u * (2 * S + a); };
+  auto aempty_b = [&](int a) { return bars + 8u * (2 * S + A + a); };
+  const uint32_t lora_full = bars + 8u * (2 * S + 2 * A);
+  const uint32_t lora_empty = lora_full + 8u;
+  auto acc_full = [&](int b) { return lora_full + 16u + 8u * b; };
+  auto acc_empty = [&](int b) { return lora_full + 32u + 8u * b; };
+  const uint32_t tmem_slot = lora_full + 48u;
   volatile uint32_t* tmem_slot_ptr =
       reinterpret_cast<volatile uint32_t*>(gbase + (tmem_slot - base));
 
@@ -237,8 +286,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full_b(s), 1);
-      mbar_init(wready_b(s), 4);
       mbar_init(empty_b(s), 1);
+    }
+    for (int a = 0; a < A; ++a) {
+      mbar_init(aready_b(a), 4);
+      mbar_init(aempty_b(a), 1);
     }
     mbar_init(lora_full, 1);
     mbar_init(lora_empty, 1);
@@ -262,6 +314,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (elect_one_sync()) {
       tma_prefetch_desc(&tm_x);
       tma_prefetch_desc(&tm_c);
+      if constexpr (STMA) {
+        tma_prefetch_desc(&tm_sc);
+        tma_prefetch_desc(&tm_bi);
+      }
       if (has_lora) {
         tma_prefetch_desc(&tm_lup);
         tma_prefetch_desc(&tm_ldn);
@@ -293,12 +349,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t ph = (it / S) & 1;
           ok = mbar_wait(empty_b(s), ph ^ 1, p.status);
           if (!ok) break;
-          mbar_arrive_expect_tx(full_b(s), C::X_BYTES + C::C_BYTES);
-          tma_load_2d(x_s(s), &tm_x, full_b(s), kk * kBK, m0);
+          const int k0 = kk * kBK;
+          mbar_arrive_expect_tx(full_b(s), C::X_BYTES + C::C_BYTES + 2 * C::SC_BYTES);
+          tma_load_2d(x_s(s), &tm_x, full_b(s), k0, m0);
           if constexpr (TRANS)
-            tma_load_2d(c_s(s), &tm_c, full_b(s), kk * kBK * BITS / 32, out0);
+            tma_load_2d(c_s(s), &tm_c, full_b(s), k0 * BITS / 32, out0);
           else
-            tma_load_2d(c_s(s), &tm_c, full_b(s), out0 * BITS / 32, kk * kBK);
+            tma_load_2d(c_s(s), &tm_c, full_b(s), out0 * BITS / 32, k0);
+          if constexpr (STMA) {
+            const int gx = scale_window<TRANS>(p, out0, k0);
+            const int gy = TRANS ? out0 : k0;
+            tma_load_2d(sc_s(s), &tm_sc, full_b(s), gx, gy);
+            tma_load_2d(bi_s(s), &tm_bi, full_b(s), gx, gy);
+          }
         }
       }
       // Never leave a copy in flight: wait for the last phase of every stage.
@@ -335,22 +398,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int kk = 0; kk < num_k; ++kk, ++it) {
           const int s = it % S;
-          const uint32_t ph = (it / S) & 1;
-          ok = mbar_wait(full_b(s), ph, p.status) && mbar_wait(wready_b(s), ph, p.status);
+          const int a = it % A;
+          ok = mbar_wait(full_b(s), (it / S) & 1, p.status) &&
+               mbar_wait(aready_b(a), (it / A) & 1, p.status);
           if (!ok) break;
           tc_fence_after();
 #pragma unroll
           for (int k4 = 0; k4 < kBK / 16; ++k4) {
             uint64_t adesc;
             if constexpr (TRANS)
-              adesc = make_sdesc(a_s(s) + k4 * 32, 16, 1024, kSw128);
+              adesc = make_sdesc(a_s(a) + k4 * 32, 16, 1024, kSw128);
             else
-              adesc = make_sdesc(a_s(s) + k4 * 2048, 8192, 1024, kSw128);
+              adesc = make_sdesc(a_s(a) + k4 * 2048, 8192, 1024, kSw128);
             const uint64_t bdesc = make_sdesc(x_s(s) + k4 * 32, 16, 1024, kSw128);
             umma_bf16(d, adesc, bdesc, idesc, acc);
             acc = 1;
           }
           umma_commit(empty_b(s));
+          umma_commit(aempty_b(a));
         }
         umma_commit(acc_full(buf));
       }
@@ -362,38 +427,66 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------- dequant warps
     const int t = threadIdx.x - 64;  // 0..127
     const int total = my_tiles * num_k;
-    GroupPair ring[kRing];
     auto coords = [&](int j, int& out0, int& k0) {
       const int lt = j / num_k;
       out0 = tile_out0(lt);
       k0 = (j - lt * num_k) * kBK;
     };
-#pragma unroll
-    for (int u = 0; u < kRing - 1; ++u) {
-      if (u < total) {
+    auto step = [&](int j, const uint32_t (&s2)[2], const uint32_t (&b2)[2]) -> bool {
+      (void)s2;
+      const int s = j % S;
+      const int a = j % A;
+      if (!mbar_wait(full_b(s), (j / S) & 1, p.status)) return false;
+      if (!mbar_wait(aempty_b(a), ((j / A) & 1) ^ 1, p.status)) return false;
+      uint32_t ss[2] = {s2[0], s2[1]}, bb[2] = {b2[0], b2[1]};
+      if constexpr (STMA) {
         int out0, k0;
-        coords(u, out0, k0);
-        ring[u] = load_groups<TRANS>(p, t, out0, k0);
+        coords(j, out0, k0);
+        const GroupCoord gc = group_coord<TRANS>(p, t, out0, k0);
+        const uint32_t gx = static_cast<uint32_t>(scale_window<TRANS>(p, out0, k0));
+        const uint32_t row = TRANS ? static_cast<uint32_t>(t) : static_cast<uint32_t>(t & 63);
+        const uint32_t o0 = row * 16 + (gc.g0 - gx) * 2;
+        const uint32_t o1 = row * 16 + (gc.g1 - gx) * 2;
+        ss[0] = bf16_dup(static_cast<uint16_t>(lds_u16(sc_s(s) + o0)));
+        bb[0] = bf16_dup(static_cast<uint16_t>(lds_u16(bi_s(s) + o0)));
+        ss[1] = bf16_dup(static_cast<uint16_t>(lds_u16(sc_s(s) + o1)));
+        bb[1] = bf16_dup(static_cast<uint16_t>(lds_u16(bi_s(s) + o1)));
       }
-    }
-    bool ok = true;
-    for (int j0 = 0; j0 < total && ok; j0 += kRing) {
+      dequant_tile<BITS, TRANS>(c_s(s), a_s(a), t, ss, bb);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(aready_b(a));
+      return true;
+    };
+    if constexpr (STMA) {
+      const uint32_t none[2] = {0u, 0u};
+      for (int j = 0; j < total; ++j)
+        if (!step(j, none, none)) break;
+    } else {
+      GroupRaw ring[kRing];
 #pragma unroll
-      for (int u = 0; u < kRing; ++u) {
-        const int j = j0 + u;
-        if (j < total && ok) {
-          if (j + kRing - 1 < total) {
-            int out0, k0;
-            coords(j + kRing - 1, out0, k0);
-            ring[(u + kRing - 1) % kRing] = load_groups<TRANS>(p, t, out0, k0);
-          }
-          const int s = j % S;
-          ok = mbar_wait(full_b(s), (j / S) & 1, p.status);
-          if (ok) {
-            dequant_tile<BITS, TRANS>(c_s(s), a_s(s), t, ring[u]);
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(wready_b(s));
+      for (int u = 0; u < kRing - 1; ++u) {
+        if (u < total) {
+          int out0, k0;
+          coords(u, out0, k0);
+          ring[u] = load_groups<TRANS>(p, t, out0, k0);
+        }
+      }
+      bool ok = true;
+      for (int j0 = 0; j0 < total && ok; j0 += kRing) {
+#pragma unroll
+        for (int u = 0; u < kRing; ++u) {
+          const int j = j0 + u;
+          if (j < total && ok) {
+            if (j + kRing - 1 < total) {
+              int out0, k0;
+              coords(j + kRing - 1, out0, k0);
+              ring[(u + kRing - 1) % kRing] = load_groups<TRANS>(p, t, out0, k0);
+            }
+            const GroupRaw& g = ring[u];
+            const uint32_t s2[2] = {widen(g.s0, g.s0), widen(g.s1, g.s1)};
+            const uint32_t b2[2] = {widen(g.b0, g.s0), widen(g.b1, g.s1)};
+            ok = step(j, s2, b2);
           }
         }
       }
@@ -458,12 +551,12 @@ struct Args {
   void* y;
 };
 
-template <int BITS, bool TRANS, int BN>
+template <int BITS, bool TRANS, int BN, bool STMA>
 int launch(const Args& a, cudaStream_t stream, int* status) {
-  using C = Cfg<BITS, TRANS, BN>;
+  using C = Cfg<BITS, TRANS, BN, STMA>;
   const int64_t k_red = TRANS ? a.w_cols : a.w_rows;
   const int64_t n_out = TRANS ? a.w_rows : a.w_cols;
-  CUtensorMap tm_x, tm_c, tm_lup, tm_ldn;
+  CUtensorMap tm_x, tm_c, tm_lup, tm_ldn, tm_sc, tm_bi;
   int rc;
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(k_red), static_cast<uint64_t>(a.m)};
@@ -490,6 +583,21 @@ int launch(const Args& a, cudaStream_t stream, int* status) {
     }
     rc = encode_tmap(&tm_c, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, a.codes, dims, strides, box, sw);
     if (rc) return rc;
+  }
+  if constexpr (STMA) {
+    const uint64_t gpr = static_cast<uint64_t>(a.w_cols / a.group_size);
+    const uint64_t dims[2] = {gpr, static_cast<uint64_t>(a.w_rows)};
+    const uint64_t strides[1] = {gpr * 2};
+    const uint32_t box[2] = {8, static_cast<uint32_t>(C::SC_ROWS)};
+    rc = encode_tmap(&tm_sc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.scales, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    rc = encode_tmap(&tm_bi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.biases, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  } else {
+    tm_sc = tm_x;
+    tm_bi = tm_x;
   }
   if (a.rank > 0) {
     if constexpr (TRANS) {
@@ -532,13 +640,24 @@ int launch(const Args& a, cudaStream_t stream, int* status) {
   const int64_t tiles_m = (a.m + BN - 1) / BN;
   p.tiles_total = static_cast<int>(p.tiles_n * tiles_m);
   p.status = status;
-  auto kernel = qmm_kernel<BITS, TRANS, BN>;
+  auto kernel = qmm_kernel<BITS, TRANS, BN, STMA>;
   rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
                   "cudaFuncSetAttribute(qmm smem)");
   if (rc) return rc;
   const int grid = p.tiles_total < sm_count() ? p.tiles_total : sm_count();
-  kernel<<<grid, kThreads, C::SMEM, stream>>>(tm_x, tm_c, tm_lup, tm_ldn, p);
+  kernel<<<grid, kThreads, C::SMEM, stream>>>(tm_x, tm_c, tm_lup, tm_ldn, tm_sc, tm_bi, p);
   return check_cuda(cudaGetLastError(), "qmm launch");
+}
+
+// The scale/bias tiles ride in the TMA stages when their rows start on
+// 16-byte boundaries (groups per row a multiple of 8, 16-byte aligned base);
+// otherwise each dequantizing thread loads its own.
+template <int BITS, bool TRANS, int BN>
+int launch_scales(const Args& a, cudaStream_t stream, int* status) {
+  const int64_t gpr = a.w_cols / a.group_size;
+  const bool stma = gpr % 8 == 0 && aligned(a.scales, 16) && aligned(a.biases, 16);
+  return stma ? launch<BITS, TRANS, BN, true>(a, stream, status)
+              : launch<BITS, TRANS, BN, false>(a, stream, status);
 }
 
 template <int BITS, bool TRANS>
@@ -566,10 +685,10 @@ int launch_bn(const Args& a, cudaStream_t stream, int* status) {
   if (bn == 32 && a.m > 32) bn = a.m > 128 ? 128 : 64;
   }
   switch (bn) {
-    case 256: return launch<BITS, TRANS, 256>(a, stream, status);
-    case 128: return launch<BITS, TRANS, 128>(a, stream, status);
-    case 64: return launch<BITS, TRANS, 64>(a, stream, status);
-    default: return launch<BITS, TRANS, 32>(a, stream, status);
+    case 256: return launch_scales<BITS, TRANS, 256>(a, stream, status);
+    case 128: return launch_scales<BITS, TRANS, 128>(a, stream, status);
+    case 64: return launch_scales<BITS, TRANS, 64>(a, stream, status);
+    default: return launch_scales<BITS, TRANS, 32>(a, stream, status);
   }
 }
 
