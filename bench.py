@@ -159,6 +159,8 @@ def cpu_port_tokens_per_s(cfg, tokens: int, reps: int = 1):
 
     from oracle import oracle as O
 
+    # torchrun sets OMP_NUM_THREADS=1 per rank; the baseline uses every core.
+    O.set_threads(os.cpu_count() or 1)
     rng = np.random.default_rng(7)
     shapes = cfg.linear_shapes()
     qw = {}
