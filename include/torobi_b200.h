@@ -176,6 +176,43 @@ int tq_adamw(float* params, const float* grads, float* m, float* v, int64_t n, i
  */
 int tq_transpose_to_bf16(const float* src, int64_t rows, int64_t cols, void* dst, void* stream);
 
+/* -------------------------------------------------------- decoder glue --- */
+/*
+ * The decoder operations around the quantized linears, fused (bf16 in and
+ * out, f32 arithmetic).  Not part of the quantized-weight path itself; they
+ * replace the reference's composed ops for the Llama-shaped block.
+ *
+ * RMSNorm over the last axis (engine/src/interp.rs:312-319):
+ *   y = x * rsqrt(mean(x^2) + eps) * w; rstd (optional, f32 [rows]) keeps
+ *   rsqrt(mean(x^2) + eps) for the backward.  hidden % 8 == 0.
+ */
+int tq_rmsnorm_fwd(const void* x, const void* w, int64_t rows, int64_t hidden, float eps, void* y,
+                   float* rstd, void* stream);
+
+/*
+ * Its input gradient (the gain is frozen in QLoRA, so no dw):
+ *   dx = rstd * dy * w - x * rstd^3 * mean(dy * w * x)  (+ dres, if not NULL).
+ */
+int tq_rmsnorm_bwd(const void* x, const void* w, const float* rstd, const void* dy,
+                   const void* dres, int64_t rows, int64_t hidden, void* dx, void* stream);
+
+/*
+ * Rotary embedding in place or out of place on x [tokens, heads, dim] bf16
+ * (tokens = batch * seq, position = token % seq): the first half of each head
+ * rotates against the second, by the angles whose cos/sin are [seq, dim/2]
+ * f32 (engine/src/interp.rs:350-388).  inverse != 0 rotates back (the VJP).
+ */
+int tq_rope(const void* x, int64_t tokens, int64_t heads, int64_t dim, int64_t seq,
+            const float* cos_table, const float* sin_table, int inverse, void* y, void* stream);
+
+/*
+ * SwiGLU (lib/torobi/models/llama.rb:320-327): a = g * sigmoid(g) * u over n
+ * elements, and its VJP dg, du.  n % 8 == 0.
+ */
+int tq_swiglu_fwd(const void* g, const void* u, int64_t n, void* a, void* stream);
+int tq_swiglu_bwd(const void* g, const void* u, const void* da, int64_t n, void* dg, void* du,
+                  void* stream);
+
 /* ------------------------------------------------------ data parallel ---- */
 /*
  * NCCL communicator for the data-parallel step (no reference counterpart:

@@ -63,6 +63,11 @@ SIGNATURES = {
     "tq_adamw": ([_vp, _vp, _vp, _vp, _i64, _i64, _f32, _f32, _f32, _f32, _f32, _f32, _vp, _f32,
                   _vp, _vp], _i32),
     "tq_transpose_to_bf16": ([_vp, _i64, _i64, _vp, _vp], _i32),
+    "tq_rmsnorm_fwd": ([_vp, _vp, _i64, _i64, _f32, _vp, _vp, _vp], _i32),
+    "tq_rmsnorm_bwd": ([_vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp], _i32),
+    "tq_rope": ([_vp, _i64, _i64, _i64, _i64, _vp, _vp, _i32, _vp, _vp], _i32),
+    "tq_swiglu_fwd": ([_vp, _vp, _i64, _vp, _vp], _i32),
+    "tq_swiglu_bwd": ([_vp, _vp, _vp, _i64, _vp, _vp, _vp], _i32),
     "tq_dp_unique_id": ([_vp], _i32),
     "tq_dp_comm_init": ([ctypes.POINTER(_vp), _vp, _i32, _i32], _i32),
     "tq_dp_allreduce_sum": ([_vp, _vp, _i64, _i32, _vp], _i32),

@@ -1,0 +1,109 @@
+"""Fused decoder glue as differentiable ops: RMSNorm, rotary embedding and
+SwiGLU, each one sm_100a kernel forward and one backward (csrc/glue.cu).
+
+RMSNorm is ``x * rsqrt(mean(x^2) + eps) * w`` (engine/src/interp.rs:312-319),
+with a frozen gain; RoPE rotates the first half of each head against the
+second (engine/src/interp.rs:350-388); SwiGLU is ``(g * sigmoid(g)) * u``
+(lib/torobi/models/llama.rb:320-327).
+"""
+from __future__ import annotations
+
+import torch
+
+from .ops import _launch, _need_cuda, _ptr, _stream
+from ._lib import lib
+
+
+def _bf16_contig(name: str, t: torch.Tensor) -> torch.Tensor:
+    if t.dtype != torch.bfloat16:
+        raise ValueError(f"{name} must be bfloat16, got {t.dtype}")
+    return t.contiguous()
+
+
+class _RMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, eps):
+        _need_cuda("rms_norm", x=x, w=w)
+        x = _bf16_contig("x", x)
+        w = _bf16_contig("w", w)
+        h = x.shape[-1]
+        rows = x.numel() // h
+        y = torch.empty_like(x)
+        rstd = torch.empty(rows, dtype=torch.float32, device=x.device)
+        _launch("rmsnorm", lambda: lib().tq_rmsnorm_fwd(_ptr(x), _ptr(w), rows, h, float(eps),
+                                                         _ptr(y), _ptr(rstd), _stream()))
+        ctx.save_for_backward(x, w, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w, rstd = ctx.saved_tensors
+        dy = dy.contiguous()
+        h = x.shape[-1]
+        rows = x.numel() // h
+        dx = torch.empty_like(x)
+        _launch("rmsnorm", lambda: lib().tq_rmsnorm_bwd(_ptr(x), _ptr(w), _ptr(rstd), _ptr(dy),
+                                                         None, rows, h, _ptr(dx), _stream()))
+        return dx, None, None
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """RMSNorm over the last axis; differentiable wrt x (the gain is frozen)."""
+    return _RMSNorm.apply(x, w, eps)
+
+
+class _RoPE(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, cos, sin, seq):
+        _need_cuda("rope", x=x, cos=cos, sin=sin)
+        x = _bf16_contig("x", x)
+        tokens, heads, dim = x.shape[0] * x.shape[1], x.shape[2], x.shape[3]
+        y = torch.empty_like(x)
+        _launch("rope", lambda: lib().tq_rope(_ptr(x), tokens, heads, dim, seq, _ptr(cos),
+                                               _ptr(sin), 0, _ptr(y), _stream()))
+        ctx.save_for_backward(cos, sin)
+        ctx.seq = seq
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        cos, sin = ctx.saved_tensors
+        dy = dy.contiguous()
+        tokens, heads, dim = dy.shape[0] * dy.shape[1], dy.shape[2], dy.shape[3]
+        dx = torch.empty_like(dy)
+        _launch("rope", lambda: lib().tq_rope(_ptr(dy), tokens, heads, dim, ctx.seq, _ptr(cos),
+                                               _ptr(sin), 1, _ptr(dx), _stream()))
+        return dx, None, None, None
+
+
+def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """x [batch, seq, heads, dim] bf16; cos/sin [seq, dim/2] f32."""
+    return _RoPE.apply(x, cos.contiguous(), sin.contiguous(), x.shape[1])
+
+
+class _SwiGLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, g, u):
+        _need_cuda("swiglu", g=g, u=u)
+        g = _bf16_contig("g", g)
+        u = _bf16_contig("u", u)
+        a = torch.empty_like(g)
+        _launch("swiglu", lambda: lib().tq_swiglu_fwd(_ptr(g), _ptr(u), g.numel(), _ptr(a),
+                                                       _stream()))
+        ctx.save_for_backward(g, u)
+        return a
+
+    @staticmethod
+    def backward(ctx, da):
+        g, u = ctx.saved_tensors
+        da = da.contiguous()
+        dg = torch.empty_like(g)
+        du = torch.empty_like(u)
+        _launch("swiglu", lambda: lib().tq_swiglu_bwd(_ptr(g), _ptr(u), _ptr(da), g.numel(),
+                                                       _ptr(dg), _ptr(du), _stream()))
+        return dg, du
+
+
+def swiglu(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
+    """(g * sigmoid(g)) * u."""
+    return _SwiGLU.apply(g, u)

@@ -13,8 +13,9 @@ over next-token targets.
 
 Every linear of every block is a ``QuantizedWeight`` (MLX affine codes) run by
 the tcgen05 quantized GEMM; adapted linears add the fused LoRA branch.  The
-glue between them (norms, RoPE, attention, SwiGLU, the bf16 head and the loss)
-is PyTorch -- it is outside the quantized-weight path this package replaces.
+norms, RoPE and SwiGLU between them are fused kernels (``glue``); attention
+(PyTorch SDPA), the bf16 head and the loss are library calls -- they are
+outside the quantized-weight path this package replaces.
 The head stays bf16 (a plain library GEMM): QLoRA quantizes the blocks'
 linears and keeps the vocabulary projection in the compute dtype.
 """
@@ -26,6 +27,7 @@ from dataclasses import dataclass, field
 import torch
 import torch.nn.functional as F
 
+from . import glue
 from .qlora import Adapter, LoRAStore, QuantizedWeight, qlora_linear
 
 LINEARS = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
@@ -102,7 +104,8 @@ def tiny_config(**over) -> DecoderConfig:
     return DecoderConfig(**base)
 
 
-def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+def rms_norm_reference(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """RMSNorm composed from PyTorch ops (the tests' f32 restatement)."""
     xf = x.float()
     scale = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
     return (xf * scale * w.float()).to(x.dtype)
@@ -117,7 +120,7 @@ def rope_tables(seq: int, dim: int, theta: float, device) -> tuple[torch.Tensor,
 
 
 def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-    """x [B, H, S, D]: the first half rotates against the second."""
+    """RoPE composed from PyTorch ops, x [B, H, S, D] (the tests' restatement)."""
     half = x.shape[-1] // 2
     xf = x.float()
     a, b = xf[..., :half], xf[..., half:]
@@ -190,30 +193,30 @@ class QLoRACausalLM:
         cfg = self.cfg
         B, S, H = x.shape
         cos, sin = self._rope(S)
-        h = rms_norm(x, blk.input_norm, cfg.rms_eps)
+        h = glue.rms_norm(x, blk.input_norm, cfg.rms_eps)
         q = qlora_linear(h, blk.linears["q_proj"], blk.adapters["q_proj"])
         k = qlora_linear(h, blk.linears["k_proj"], blk.adapters["k_proj"])
         v = qlora_linear(h, blk.linears["v_proj"], blk.adapters["v_proj"])
-        q = q.view(B, S, cfg.heads, cfg.head_dim).transpose(1, 2)
-        k = k.view(B, S, cfg.kv_heads, cfg.head_dim).transpose(1, 2)
-        v = v.view(B, S, cfg.kv_heads, cfg.head_dim).transpose(1, 2)
-        q = apply_rope(q, cos, sin)
-        k = apply_rope(k, cos, sin)
-        att = F.scaled_dot_product_attention(q, k, v, is_causal=True,
+        # [B, S, heads, D] in memory; attention reads the [B, heads, S, D] view.
+        q = glue.rope(q.view(B, S, cfg.heads, cfg.head_dim), cos, sin)
+        k = glue.rope(k.view(B, S, cfg.kv_heads, cfg.head_dim), cos, sin)
+        v = v.view(B, S, cfg.kv_heads, cfg.head_dim)
+        att = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2),
+                                             v.transpose(1, 2), is_causal=True,
                                              enable_gqa=cfg.heads != cfg.kv_heads)
         att = att.transpose(1, 2).reshape(B, S, cfg.heads * cfg.head_dim)
         x = x + qlora_linear(att, blk.linears["o_proj"], blk.adapters["o_proj"])
-        h = rms_norm(x, blk.post_norm, cfg.rms_eps)
+        h = glue.rms_norm(x, blk.post_norm, cfg.rms_eps)
         g = qlora_linear(h, blk.linears["gate_proj"], blk.adapters["gate_proj"])
         u = qlora_linear(h, blk.linears["up_proj"], blk.adapters["up_proj"])
-        a = F.silu(g) * u
-        return x + qlora_linear(a, blk.linears["down_proj"], blk.adapters["down_proj"])
+        return x + qlora_linear(glue.swiglu(g, u), blk.linears["down_proj"],
+                                blk.adapters["down_proj"])
 
     def hidden(self, ids: torch.Tensor) -> torch.Tensor:
         x = F.embedding(ids, self.embed)
         for blk in self.blocks:
             x = self.block_forward(blk, x)
-        return rms_norm(x, self.final_norm, self.cfg.rms_eps)
+        return glue.rms_norm(x, self.final_norm, self.cfg.rms_eps)
 
     def logits(self, h: torch.Tensor) -> torch.Tensor:
         head = self.embed if self.lm_head is None else self.lm_head
