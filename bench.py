@@ -426,8 +426,10 @@ def run_kernels(args):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    flush_buf = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
-    flush = lambda: flush_buf.zero_()  # noqa: E731  (256 MB > 126 MB of L2)
+    # 1 GiB (> 126 MB of L2), long enough that the host has enqueued the timed
+    # launch before the flush ends, so the events time the device only.
+    flush_buf = torch.empty(1024 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    flush = lambda: flush_buf.zero_()  # noqa: E731
     peaks, peak_kind = measured_peaks()
     burst = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
     hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))

@@ -116,6 +116,29 @@ int tq_qlora_matmul(const void* x, const void* codes, const void* scales, const 
                     int bits, const void* bias, const void* lora_up, const void* lora_down,
                     int64_t rank, void* y, void* stream);
 
+/*
+ * Split-K forms of the two GEMM entry points.  When the output tiles alone
+ * cannot occupy every SM (small m), the reduction is split across CTAs that
+ * write f32 partials into the caller's workspace; a second kernel sums them,
+ * adds the bias and rounds to bf16.  tq_qmm_workspace_bytes reports how many
+ * bytes a call of this shape needs (0: it will not split); a NULL workspace
+ * (or one too small) is refused when a split is planned.  The results equal
+ * the plain entry points' to f32 summation order.  No reference counterpart:
+ * the same replacement of mlx_matmul as tq_quantized_matmul, scheduled for
+ * small token counts.
+ */
+int tq_qmm_workspace_bytes(int64_t m, int64_t w_rows, int64_t w_cols, int transpose,
+                           int group_size, int bits, size_t* bytes);
+int tq_quantized_matmul_ws(const void* x, const void* codes, const void* scales,
+                           const void* biases, int64_t m, int64_t w_rows, int64_t w_cols,
+                           int transpose, int group_size, int bits, void* y, void* workspace,
+                           size_t workspace_bytes, void* stream);
+int tq_qlora_matmul_ws(const void* x, const void* codes, const void* scales, const void* biases,
+                       int64_t m, int64_t w_rows, int64_t w_cols, int transpose, int group_size,
+                       int bits, const void* bias, const void* lora_up, const void* lora_down,
+                       int64_t rank, void* y, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
 /* ------------------------------------------------------- LoRA side branch */
 
 /*

@@ -50,6 +50,8 @@ CASES = [
     # scale tiles staged by TMA (groups per row a multiple of 8)
     (300, 520, 1024, 16, 32.0, 4, 64, True),
     (96, 1024, 2048, 8, 16.0, 8, 32, False),
+    # small m: split-K (LoRA added by the first split only, bias by the reduce)
+    (32, 1024, 2048, 16, 32.0, 4, 64, True),
 ]
 
 

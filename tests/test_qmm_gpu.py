@@ -29,6 +29,9 @@ CASES = [
     (257, 392, 1024, 4, 32),
     (1000, 1032, 2048, 4, 128),
     (33, 264, 4096, 8, 64),
+    # small m: split-K over f32 partials in a workspace
+    (16, 4096, 4096, 4, 64),
+    (100, 2048, 2048, 8, 32),
 ]
 
 
@@ -107,3 +110,39 @@ def test_quantized_matmul_argument_errors(cuda):
         tq.quantized_matmul(torch.zeros((4, 256), dtype=torch.bfloat16, device=cuda), c, s[:, :2], b)
     y = tq.quantized_matmul(torch.zeros((0, 256), dtype=torch.bfloat16, device=cuda), c, s, b)
     assert y.shape == (0, 128)
+
+
+@pytest.mark.gpu
+def test_split_k_matches_the_unsplit_kernel(cuda):
+    """The workspace form equals the plain entry point (which never splits)
+    to f32 summation order, and refuses a workspace that is too small."""
+    import ctypes
+
+    import torch
+    import torobi_b200 as tq
+    from torobi_b200._lib import check, lib
+
+    torch.manual_seed(3)
+    m, n, k = 24, 2048, 4096
+    w = (torch.randn(n, k, device=cuda) * 0.02).bfloat16()
+    c, s, b = tq.quantize(w, 64, 4)
+    x = torch.randn(m, k, device=cuda).bfloat16()
+    nbytes = ctypes.c_size_t(0)
+    check(lib().tq_qmm_workspace_bytes(m, n, k, 1, 64, 4, ctypes.byref(nbytes)))
+    assert nbytes.value > 0
+    st = torch.cuda.current_stream().cuda_stream
+    y0 = torch.empty(m, n, device=cuda, dtype=torch.bfloat16)
+    check(lib().tq_quantized_matmul(x.data_ptr(), c.data_ptr(), s.data_ptr(), b.data_ptr(), m, n,
+                                    k, 1, 64, 4, y0.data_ptr(), st))
+    ws = torch.empty(nbytes.value, dtype=torch.uint8, device=cuda)
+    y1 = torch.empty_like(y0)
+    check(lib().tq_quantized_matmul_ws(x.data_ptr(), c.data_ptr(), s.data_ptr(), b.data_ptr(), m,
+                                       n, k, 1, 64, 4, y1.data_ptr(), ws.data_ptr(), nbytes.value,
+                                       st))
+    torch.cuda.synchronize()
+    err = ((y1.float() - y0.float()).abs().max() / y0.float().abs().max()).item()
+    assert err < 1e-2
+    rc = lib().tq_quantized_matmul_ws(x.data_ptr(), c.data_ptr(), s.data_ptr(), b.data_ptr(), m,
+                                      n, k, 1, 64, 4, y1.data_ptr(), ws.data_ptr(),
+                                      nbytes.value - 16, st)
+    assert rc != 0 and b"workspace" in lib().tq_last_error()

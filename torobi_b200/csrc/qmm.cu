@@ -13,9 +13,10 @@
 //               packed-code tile and the group scale/bias tiles of each stage;
 //               the LoRA tiles once per output tile.
 //   warp 1      TMEM allocator and the single UMMA-issuing thread.
-//   warps 2-5   dequantizers: packed codes (shared) -> bf16 weight tile in the
-//               UMMA canonical 128B-swizzled layout, w = RNE(scale*q + bias).
-//   warps 6-9   epilogue: TMEM -> registers -> (+ bias) -> bf16 -> global,
+//   warps 2-9   dequantizers (two per scheduler): packed codes (shared) -> bf16
+//               weight tile in the UMMA canonical 128B-swizzled layout,
+//               w = RNE(scale*q + bias); each thread owns 32 codes of a row.
+//   warps 10-13 epilogue: TMEM -> registers -> (+ bias) -> bf16 -> global,
 //               overlapped with the next tile (two TMEM accumulators).
 //
 // transpose (linear forward, y = x . W^T): the reduction runs along W's packed
@@ -39,7 +40,8 @@ namespace {
 
 constexpr int kBM = 128;        // weight-side rows per tile (UMMA M)
 constexpr int kBK = 64;         // reduction elements per pipeline stage
-constexpr int kThreads = 320;   // 10 warps
+constexpr int kThreads = 448;   // 14 warps
+constexpr int kDqWarps = 8;     // dequantizing warps (two per scheduler)
 constexpr int kSmemLimit = 232448;
 constexpr int kRing = 4;        // fallback path: scale/bias register ring (k-steps)
 
@@ -92,6 +94,9 @@ struct Params {
   int lora_rank;             // 0, 8 or 16
   int tiles_n;               // output tiles along n_out
   int tiles_total;           // tiles_n * tiles along m
+  int splits;                // k-splits per tile (split-K); 1 = none
+  int k_steps_per_split;     // k-steps of every split but maybe the last
+  float* ws;                 // splits > 1: f32 partials [splits, m, n_out]
   int* status;
 };
 
@@ -107,9 +112,13 @@ __device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
 
 // Groups of one k-step for dequantizing thread t (0..127): first and second
 // (group 32 splits a 64-wide step in two), and the weight row they sit on.
+// The group one dequantizing thread t (0..255) needs for one k-step, and the
+// weight row it sits on.  Forward: t covers row t % 128, k half t / 128 (32
+// codes, one group for every group size).  Backward: t covers weight row
+// k0 + t % 64 and output quarter t / 64 (32 outputs, one group).
 struct GroupCoord {
   int row;       // weight row
-  uint32_t g0, g1;
+  uint32_t g;    // group along the weight row
   bool rv;       // row inside the weight
 };
 
@@ -117,15 +126,12 @@ template <bool TRANS>
 __device__ __forceinline__ GroupCoord group_coord(const Params& p, int t, int out0, int k0) {
   GroupCoord c;
   if constexpr (TRANS) {
-    c.row = out0 + t;  // weight row = output feature
-    c.g0 = static_cast<uint32_t>(k0) >> p.group_shift;
-    c.g1 = static_cast<uint32_t>(k0 + 32) >> p.group_shift;
+    c.row = out0 + (t & 127);  // weight row = output feature
+    c.g = static_cast<uint32_t>(k0 + 32 * (t >> 7)) >> p.group_shift;
     c.rv = c.row < p.n_out;
   } else {
-    const int h = t >> 6;
     c.row = k0 + (t & 63);  // weight row = reduction index
-    c.g0 = static_cast<uint32_t>(out0 + 64 * h) >> p.group_shift;
-    c.g1 = static_cast<uint32_t>(out0 + 64 * h + 32) >> p.group_shift;
+    c.g = static_cast<uint32_t>(out0 + 32 * (t >> 6)) >> p.group_shift;
     c.rv = c.row < p.w_rows;
   }
   return c;
@@ -141,21 +147,18 @@ __device__ __forceinline__ int scale_window(const Params& p, int out0, int k0) {
 // Fallback path (scale rows not 16-byte aligned): raw bits loaded by the
 // dequantizing thread kRing-1 steps ahead; bit 16 flags out-of-range.
 struct GroupRaw {
-  uint32_t s0, b0, s1, b1;
+  uint32_t s, b;
 };
 
 template <bool TRANS>
 __device__ __forceinline__ GroupRaw load_groups(const Params& p, int t, int out0, int k0) {
   const GroupCoord c = group_coord<TRANS>(p, t, out0, k0);
   const uint32_t gpr = static_cast<uint32_t>(p.groups_per_row);
-  const size_t rb = static_cast<size_t>(c.row) * gpr;
-  const bool v0 = c.rv && c.g0 < gpr, v1 = c.rv && c.g1 < gpr;
-  const size_t i0 = v0 ? rb + c.g0 : 0, i1 = v1 ? rb + c.g1 : 0;
+  const bool v = c.rv && c.g < gpr;
+  const size_t i = v ? static_cast<size_t>(c.row) * gpr + c.g : 0;
   GroupRaw g;
-  g.s0 = ldg_u16(p.scales + i0) | (v0 ? 0u : 0x10000u);
-  g.b0 = ldg_u16(p.biases + i0);
-  g.s1 = ldg_u16(p.scales + i1) | (v1 ? 0u : 0x10000u);
-  g.b1 = ldg_u16(p.biases + i1);
+  g.s = ldg_u16(p.scales + i) | (v ? 0u : 0x10000u);
+  g.b = ldg_u16(p.biases + i);
   return g;
 }
 
@@ -164,65 +167,67 @@ __device__ __forceinline__ uint32_t widen(uint32_t raw, uint32_t flag_from) {
 }
 
 // Packed codes (shared, as TMA left them) -> bf16 weight tile in the UMMA's
-// 128B-swizzled canonical layout.  t = dequantizing thread (0..127); s2/b2
-// the bf16 scale/bias pairs of its first and second group.
+// 128B-swizzled canonical layout.  t = dequantizing thread (0..255) owns 32
+// codes of one weight row; s2/b2 its group's bf16 scale/bias pair.
 template <int BITS, bool TRANS>
-__device__ __forceinline__ void dequant_tile(uint32_t cb, uint32_t ab, int t, const uint32_t (&s2)[2],
-                                             const uint32_t (&b2)[2]) {
+__device__ __forceinline__ void dequant_tile(uint32_t cb, uint32_t ab, int t, uint32_t s2,
+                                             uint32_t b2) {
   if constexpr (TRANS) {
-    // K-major: row r = output feature, 64 k per row (8 chunks of 16 B).
-    const int r = t;
+    // K-major: row r = output feature, k half hh; chunks 4hh..4hh+3 of the
+    // row's eight 16-byte chunks.
+    const int r = t & 127;
+    const int hh = t >> 7;
     if constexpr (BITS == 4) {
-      uint32_t w[8];
-      lds128(cb + swz<32>(r * 32), w[0], w[1], w[2], w[3]);
-      lds128(cb + swz<32>(r * 32 + 16), w[4], w[5], w[6], w[7]);
+      uint32_t w[4];
+      lds128(cb + swz<32>(r * 32 + hh * 16), w[0], w[1], w[2], w[3]);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < 4; ++j) {
         uint32_t o[4];
-        dequant_u4x8(w[j], s2[j >> 2], b2[j >> 2], o);
-        sts128(ab + r * 128 + ((j ^ (r & 7)) << 4), o[0], o[1], o[2], o[3]);
+        dequant_u4x8(w[j], s2, b2, o);
+        sts128(ab + r * 128 + (((4 * hh + j) ^ (r & 7)) << 4), o[0], o[1], o[2], o[3]);
       }
     } else {
-      uint32_t w[16];
+      uint32_t w[8];
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-        lds128(cb + swz<64>(r * 64 + c * 16), w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+      for (int c = 0; c < 2; ++c)
+        lds128(cb + swz<64>(r * 64 + (2 * hh + c) * 16), w[4 * c], w[4 * c + 1], w[4 * c + 2],
+               w[4 * c + 3]);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < 4; ++j) {
         uint32_t o0[2], o1[2];
-        dequant_u8x4(w[2 * j], s2[j >> 2], b2[j >> 2], o0);
-        dequant_u8x4(w[2 * j + 1], s2[j >> 2], b2[j >> 2], o1);
-        sts128(ab + r * 128 + ((j ^ (r & 7)) << 4), o0[0], o0[1], o1[0], o1[1]);
+        dequant_u8x4(w[2 * j], s2, b2, o0);
+        dequant_u8x4(w[2 * j + 1], s2, b2, o1);
+        sts128(ab + r * 128 + (((4 * hh + j) ^ (r & 7)) << 4), o0[0], o0[1], o1[0], o1[1]);
       }
     }
   } else {
-    // MN-major: kr = reduction row (0..63), h = which 64 outputs; atoms of
-    // 64 outputs x 8 reduction rows, 8 K-groups per 64-output block.
+    // MN-major: kr = reduction row (0..63), qq = output quarter (32 outputs);
+    // atoms of 64 outputs x 8 reduction rows, 8 K-groups per 64-output block.
     const int kr = t & 63;
-    const int h = t >> 6;
-    const uint32_t row_off = h * 8192 + (kr >> 3) * 1024 + (kr & 7) * 128;
+    const int qq = t >> 6;
+    const uint32_t row_off = (qq >> 1) * 8192 + (kr >> 3) * 1024 + (kr & 7) * 128;
+    const int j0 = (qq & 1) * 4;  // first 16-byte chunk within the 64-output atom row
     if constexpr (BITS == 4) {
-      uint32_t w[8];
-      lds128(cb + swz<64>(kr * 64 + (2 * h) * 16), w[0], w[1], w[2], w[3]);
-      lds128(cb + swz<64>(kr * 64 + (2 * h + 1) * 16), w[4], w[5], w[6], w[7]);
+      uint32_t w[4];
+      lds128(cb + swz<64>(kr * 64 + qq * 16), w[0], w[1], w[2], w[3]);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < 4; ++j) {
         uint32_t o[4];
-        dequant_u4x8(w[j], s2[j >> 2], b2[j >> 2], o);
-        sts128(ab + row_off + ((j ^ (kr & 7)) << 4), o[0], o[1], o[2], o[3]);
+        dequant_u4x8(w[j], s2, b2, o);
+        sts128(ab + row_off + (((j0 + j) ^ (kr & 7)) << 4), o[0], o[1], o[2], o[3]);
       }
     } else {
-      uint32_t w[16];
+      uint32_t w[8];
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-        lds128(cb + swz<128>(kr * 128 + (4 * h + c) * 16), w[4 * c], w[4 * c + 1], w[4 * c + 2],
-               w[4 * c + 3]);
+      for (int c = 0; c < 2; ++c)
+        lds128(cb + swz<128>(kr * 128 + (2 * qq + c) * 16), w[4 * c], w[4 * c + 1],
+               w[4 * c + 2], w[4 * c + 3]);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < 4; ++j) {
         uint32_t o0[2], o1[2];
-        dequant_u8x4(w[2 * j], s2[j >> 2], b2[j >> 2], o0);
-        dequant_u8x4(w[2 * j + 1], s2[j >> 2], b2[j >> 2], o1);
-        sts128(ab + row_off + ((j ^ (kr & 7)) << 4), o0[0], o0[1], o1[0], o1[1]);
+        dequant_u8x4(w[2 * j], s2, b2, o0);
+        dequant_u8x4(w[2 * j + 1], s2, b2, o1);
+        sts128(ab + row_off + (((j0 + j) ^ (kr & 7)) << 4), o0[0], o0[1], o1[0], o1[1]);
       }
     }
   }
@@ -271,11 +276,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_k = (p.k_red + kBK - 1) / kBK;
   const bool has_lora = p.lora_rank > 0;
   const int lora_chunks = p.lora_rank / 8;
-  const int my_tiles = static_cast<int>(blockIdx.x) < p.tiles_total
-                           ? (p.tiles_total - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1
+  // Work units: (tile, k-split) pairs, unit u = tile * splits + split, so a
+  // tile's splits run side by side.  CTA b takes units b, b + grid, ...
+  const int units_total = p.tiles_total * p.splits;
+  const int my_tiles = static_cast<int>(blockIdx.x) < units_total
+                           ? (units_total - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1
                            : 0;
-  auto tile_out0 = [&](int lt) { return ((blockIdx.x + lt * gridDim.x) % p.tiles_n) * kBM; };
-  auto tile_m0 = [&](int lt) { return ((blockIdx.x + lt * gridDim.x) / p.tiles_n) * BN; };
+  auto unit_tile = [&](int lt) {
+    return static_cast<int>((blockIdx.x + lt * gridDim.x) / p.splits);
+  };
+  auto unit_split = [&](int lt) {
+    return static_cast<int>((blockIdx.x + lt * gridDim.x) % p.splits);
+  };
+  auto tile_out0 = [&](int lt) { return (unit_tile(lt) % p.tiles_n) * kBM; };
+  auto tile_m0 = [&](int lt) { return (unit_tile(lt) / p.tiles_n) * BN; };
+  auto k_first = [&](int lt) { return unit_split(lt) * p.k_steps_per_split; };
+  auto k_count = [&](int lt) {
+    const int b = k_first(lt);
+    const int e = b + p.k_steps_per_split < num_k ? b + p.k_steps_per_split : num_k;
+    return e - b;
+  };
+  // Only split 0 of a tile adds the LoRA branch.
+  auto unit_lora = [&](int lt) { return has_lora && unit_split(lt) == 0; };
 
   // Zero the LoRA tiles once: with rank 8 the second K-chunk stays zero.
   if (has_lora) {
@@ -289,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(empty_b(s), 1);
     }
     for (int a = 0; a < A; ++a) {
-      mbar_init(aready_b(a), 4);
+      mbar_init(aready_b(a), kDqWarps);
       mbar_init(aempty_b(a), 1);
     }
     mbar_init(lora_full, 1);
@@ -327,8 +349,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int lora_loads = 0;
       for (int lt = 0; lt < my_tiles && ok; ++lt) {
         const int out0 = tile_out0(lt), m0 = tile_m0(lt);
-        if (has_lora) {
-          ok = mbar_wait(lora_empty, (lt & 1) ^ 1, p.status);
+        if (unit_lora(lt)) {
+          ok = mbar_wait(lora_empty, (lora_loads & 1) ^ 1, p.status);
           if (!ok) break;
           mbar_arrive_expect_tx(lora_full, lora_chunks * (kBM * 16 + BN * 16));
           for (int ch = 0; ch < lora_chunks; ++ch) {
@@ -344,7 +366,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           ++lora_loads;
         }
-        for (int kk = 0; kk < num_k; ++kk, ++it) {
+        const int kb = k_first(lt), ke = kb + k_count(lt);
+        for (int kk = kb; kk < ke; ++kk, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
           ok = mbar_wait(empty_b(s), ph ^ 1, p.status);
@@ -375,6 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc = make_idesc_bf16(kBM, BN, !TRANS, false);
       bool ok = true;
       int it = 0;
+      int lora_uses = 0;
       for (int lt = 0; lt < my_tiles && ok; ++lt) {
         const int buf = lt & 1;
         ok = mbar_wait(acc_empty(buf), ((lt >> 1) & 1) ^ 1, p.status);
@@ -382,8 +406,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d = tmem + buf * C::ACC_COLS;
         uint32_t acc = 0;
-        if (has_lora) {
-          ok = mbar_wait(lora_full, lt & 1, p.status);
+        if (unit_lora(lt)) {
+          ok = mbar_wait(lora_full, lora_uses & 1, p.status);
+          ++lora_uses;
           if (!ok) break;
           tc_fence_after();
           uint64_t adesc;
@@ -396,7 +421,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_commit(lora_empty);
           acc = 1;
         }
-        for (int kk = 0; kk < num_k; ++kk, ++it) {
+        const int kc = k_count(lt);
+        for (int kk = 0; kk < kc; ++kk, ++it) {
           const int s = it % S;
           const int a = it % A;
           ok = mbar_wait(full_b(s), (it / S) & 1, p.status) &&
@@ -423,45 +449,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (my_tiles > 0)
         mbar_wait(acc_full((my_tiles - 1) & 1), ((my_tiles - 1) >> 1) & 1, p.status);
     }
-  } else if (warp < 6) {
+  } else if (warp < 2 + kDqWarps) {
     // ---------------------------------------------------- dequant warps
-    const int t = threadIdx.x - 64;  // 0..127
+    const int t = threadIdx.x - 64;  // 0..255
+    // Split-K is only used with STMA, so on the fallback path every unit has
+    // num_k steps and a flat step index maps back to (unit, k-step).
     const int total = my_tiles * num_k;
     auto coords = [&](int j, int& out0, int& k0) {
       const int lt = j / num_k;
       out0 = tile_out0(lt);
       k0 = (j - lt * num_k) * kBK;
     };
-    auto step = [&](int j, const uint32_t (&s2)[2], const uint32_t (&b2)[2]) -> bool {
-      (void)s2;
+    auto step = [&](int j, int out0, int k0, uint32_t s2, uint32_t b2) -> bool {
       const int s = j % S;
       const int a = j % A;
       if (!mbar_wait(full_b(s), (j / S) & 1, p.status)) return false;
       if (!mbar_wait(aempty_b(a), ((j / A) & 1) ^ 1, p.status)) return false;
-      uint32_t ss[2] = {s2[0], s2[1]}, bb[2] = {b2[0], b2[1]};
       if constexpr (STMA) {
-        int out0, k0;
-        coords(j, out0, k0);
+        // This thread's scale and bias from the stage's 8-group tiles.
         const GroupCoord gc = group_coord<TRANS>(p, t, out0, k0);
         const uint32_t gx = static_cast<uint32_t>(scale_window<TRANS>(p, out0, k0));
-        const uint32_t row = TRANS ? static_cast<uint32_t>(t) : static_cast<uint32_t>(t & 63);
-        const uint32_t o0 = row * 16 + (gc.g0 - gx) * 2;
-        const uint32_t o1 = row * 16 + (gc.g1 - gx) * 2;
-        ss[0] = bf16_dup(static_cast<uint16_t>(lds_u16(sc_s(s) + o0)));
-        bb[0] = bf16_dup(static_cast<uint16_t>(lds_u16(bi_s(s) + o0)));
-        ss[1] = bf16_dup(static_cast<uint16_t>(lds_u16(sc_s(s) + o1)));
-        bb[1] = bf16_dup(static_cast<uint16_t>(lds_u16(bi_s(s) + o1)));
+        const uint32_t row = TRANS ? static_cast<uint32_t>(t & 127) : static_cast<uint32_t>(t & 63);
+        const uint32_t off = row * 16 + (gc.g - gx) * 2;
+        s2 = bf16_dup(static_cast<uint16_t>(lds_u16(sc_s(s) + off)));
+        b2 = bf16_dup(static_cast<uint16_t>(lds_u16(bi_s(s) + off)));
       }
-      dequant_tile<BITS, TRANS>(c_s(s), a_s(a), t, ss, bb);
+      dequant_tile<BITS, TRANS>(c_s(s), a_s(a), t, s2, b2);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(aready_b(a));
       return true;
     };
     if constexpr (STMA) {
-      const uint32_t none[2] = {0u, 0u};
-      for (int j = 0; j < total; ++j)
-        if (!step(j, none, none)) break;
+      int j = 0;
+      bool ok = true;
+      for (int lt = 0; lt < my_tiles && ok; ++lt) {
+        const int out0 = tile_out0(lt), kb = k_first(lt), kc = k_count(lt);
+        for (int kk = 0; kk < kc && ok; ++kk, ++j) ok = step(j, out0, (kb + kk) * kBK, 0u, 0u);
+      }
     } else {
       GroupRaw ring[kRing];
 #pragma unroll
@@ -484,9 +509,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               ring[(u + kRing - 1) % kRing] = load_groups<TRANS>(p, t, out0, k0);
             }
             const GroupRaw& g = ring[u];
-            const uint32_t s2[2] = {widen(g.s0, g.s0), widen(g.s1, g.s1)};
-            const uint32_t b2[2] = {widen(g.b0, g.s0), widen(g.b1, g.s1)};
-            ok = step(j, s2, b2);
+            int out0, k0;
+            coords(j, out0, k0);
+            ok = step(j, out0, k0, widen(g.s, g.s), widen(g.b, g.s));
           }
         }
       }
@@ -513,12 +538,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_wait();
         if (ok && og < p.n_out) {
           const int mlim = p.m - (m0 + c0);
-          uint16_t* yp = p.y + static_cast<size_t>(m0 + c0) * p.n_out + og;
+          if (p.splits > 1) {
+            // f32 partial of this split; the reduce kernel adds bias and rounds.
+            float* wp = p.ws + (static_cast<size_t>(unit_split(lt)) * p.m + m0 + c0) * p.n_out + og;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (j < mlim)
-              yp[static_cast<size_t>(j) * p.n_out] =
-                  __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[j]) + bias));
+            for (int j = 0; j < 32; ++j)
+              if (j < mlim) wp[static_cast<size_t>(j) * p.n_out] = __uint_as_float(v[j]);
+          } else {
+            uint16_t* yp = p.y + static_cast<size_t>(m0 + c0) * p.n_out + og;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (j < mlim)
+                yp[static_cast<size_t>(j) * p.n_out] =
+                    __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[j]) + bias));
+            }
           }
         }
       }
@@ -549,10 +582,104 @@ struct Args {
   int transpose, group_size, bits;
   int rank;
   void* y;
+  void* ws = nullptr;        // split-K workspace (f32), or null: no split
+  size_t ws_bytes = 0;
 };
 
+// How a call is run: the token tile, whether the scale tiles ride in the TMA
+// stages, and the k-split.  The workspace query and the launch share it.
+struct Plan {
+  int bn = 32;
+  bool stma = false;
+  int splits = 1;
+  int k_steps_per_split = 1;
+  size_t ws_bytes = 0;
+};
+
+int pick_bn(int64_t m, int64_t n_out) {
+  const int64_t tiles_n = (n_out + kBM - 1) / kBM;
+  const int sms = sm_count();
+  // TQ_QMM_BN pins the token tile (256, 128, 64 or 32) for tuning runs.
+  static const int forced = [] {
+    const char* e = getenv("TQ_QMM_BN");
+    return e ? atoi(e) : 0;
+  }();
+  if (forced == 256 || forced == 128 || forced == 64 || forced == 32) return forced;
+  // Largest token tile that still gives every SM a tile (M-side padding is
+  // zero-filled by TMA and never stored).
+  for (int cand : {256, 128, 64}) {
+    if (m >= cand / 2 && ((m + cand - 1) / cand) * tiles_n >= sms) return cand;
+  }
+  if (m > 128) return 128;
+  if (m > 32) return 64;
+  return 32;
+}
+
+Plan make_plan(const Args& a, bool allow_split) {
+  Plan pl;
+  const int64_t n_out = a.transpose ? a.w_rows : a.w_cols;
+  const int64_t k_red = a.transpose ? a.w_cols : a.w_rows;
+  pl.bn = pick_bn(a.m, n_out);
+  const int64_t gpr = a.w_cols / a.group_size;
+  pl.stma = gpr % 8 == 0 && aligned(a.scales, 16) && aligned(a.biases, 16);
+  const int num_k = static_cast<int>((k_red + kBK - 1) / kBK);
+  pl.k_steps_per_split = num_k;
+  if (allow_split && pl.stma) {
+    const int64_t tiles = ((n_out + kBM - 1) / kBM) * ((a.m + pl.bn - 1) / pl.bn);
+    const int sms = sm_count();
+    if (tiles < sms && num_k >= 8) {
+      int splits = static_cast<int>((sms + tiles - 1) / tiles);
+      const int max_splits = num_k / 4 < 16 ? num_k / 4 : 16;  // >= 4 k-steps per split
+      if (splits > max_splits) splits = max_splits;
+      if (splits > 1) {
+        const int per = (num_k + splits - 1) / splits;
+        pl.splits = (num_k + per - 1) / per;
+        pl.k_steps_per_split = per;
+        pl.ws_bytes = static_cast<size_t>(pl.splits) * a.m * n_out * sizeof(float);
+      }
+    }
+  }
+  return pl;
+}
+
+// y[m, n] = bf16(sum over splits of ws[s, m, n] + bias[n]); 8 outputs a thread.
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ ws,
+                                                            int splits, int64_t m, int n,
+                                                            const uint16_t* __restrict__ bias,
+                                                            uint16_t* __restrict__ y) {
+  const int64_t nv = m * n / 8;
+  const int64_t plane = m * n;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nv; v += stride) {
+    const int64_t e = v * 8;
+    float acc[8];
+    const float4* p0 = reinterpret_cast<const float4*>(ws + e);
+    float4 a0 = __ldg(p0), a1 = __ldg(p0 + 1);
+    acc[0] = a0.x; acc[1] = a0.y; acc[2] = a0.z; acc[3] = a0.w;
+    acc[4] = a1.x; acc[5] = a1.y; acc[6] = a1.z; acc[7] = a1.w;
+    for (int sp = 1; sp < splits; ++sp) {
+      const float4* ps = reinterpret_cast<const float4*>(ws + sp * plane + e);
+      a0 = __ldg(ps);
+      a1 = __ldg(ps + 1);
+      acc[0] += a0.x; acc[1] += a0.y; acc[2] += a0.z; acc[3] += a0.w;
+      acc[4] += a1.x; acc[5] += a1.y; acc[6] += a1.z; acc[7] += a1.w;
+    }
+    if (bias) {
+      const int col = static_cast<int>(e % n);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += __uint_as_float(uint32_t(__ldg(bias + col + j)) << 16);
+    }
+    uint4 o;
+    o.x = pack_bf16x2_f32(acc[0], acc[1]);
+    o.y = pack_bf16x2_f32(acc[2], acc[3]);
+    o.z = pack_bf16x2_f32(acc[4], acc[5]);
+    o.w = pack_bf16x2_f32(acc[6], acc[7]);
+    reinterpret_cast<uint4*>(y)[v] = o;
+  }
+}
+
 template <int BITS, bool TRANS, int BN, bool STMA>
-int launch(const Args& a, cudaStream_t stream, int* status) {
+int launch(const Args& a, const Plan& pl, cudaStream_t stream, int* status) {
   using C = Cfg<BITS, TRANS, BN, STMA>;
   const int64_t k_red = TRANS ? a.w_cols : a.w_rows;
   const int64_t n_out = TRANS ? a.w_rows : a.w_cols;
@@ -639,60 +766,48 @@ int launch(const Args& a, cudaStream_t stream, int* status) {
   p.tiles_n = static_cast<int>((n_out + kBM - 1) / kBM);
   const int64_t tiles_m = (a.m + BN - 1) / BN;
   p.tiles_total = static_cast<int>(p.tiles_n * tiles_m);
+  p.splits = pl.splits;
+  p.k_steps_per_split = pl.k_steps_per_split;
+  p.ws = static_cast<float*>(a.ws);
   p.status = status;
   auto kernel = qmm_kernel<BITS, TRANS, BN, STMA>;
   rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
                   "cudaFuncSetAttribute(qmm smem)");
   if (rc) return rc;
-  const int grid = p.tiles_total < sm_count() ? p.tiles_total : sm_count();
+  const int units = p.tiles_total * p.splits;
+  const int grid = units < sm_count() ? units : sm_count();
   kernel<<<grid, kThreads, C::SMEM, stream>>>(tm_x, tm_c, tm_lup, tm_ldn, tm_sc, tm_bi, p);
-  return check_cuda(cudaGetLastError(), "qmm launch");
+  rc = check_cuda(cudaGetLastError(), "qmm launch");
+  if (rc || pl.splits == 1) return rc;
+  const int64_t nv = a.m * n_out / 8;
+  int rgrid = static_cast<int>((nv + 255) / 256);
+  if (rgrid > sm_count() * 8) rgrid = sm_count() * 8;
+  splitk_reduce_kernel<<<rgrid, 256, 0, stream>>>(
+      static_cast<const float*>(a.ws), pl.splits, a.m, static_cast<int>(n_out),
+      static_cast<const uint16_t*>(a.bias), static_cast<uint16_t*>(a.y));
+  return check_cuda(cudaGetLastError(), "split-K reduce launch");
 }
 
-// The scale/bias tiles ride in the TMA stages when their rows start on
-// 16-byte boundaries (groups per row a multiple of 8, 16-byte aligned base);
-// otherwise each dequantizing thread loads its own.
 template <int BITS, bool TRANS, int BN>
-int launch_scales(const Args& a, cudaStream_t stream, int* status) {
-  const int64_t gpr = a.w_cols / a.group_size;
-  const bool stma = gpr % 8 == 0 && aligned(a.scales, 16) && aligned(a.biases, 16);
-  return stma ? launch<BITS, TRANS, BN, true>(a, stream, status)
-              : launch<BITS, TRANS, BN, false>(a, stream, status);
+int launch_scales(const Args& a, const Plan& pl, cudaStream_t stream, int* status) {
+  // The scale/bias tiles ride in the TMA stages when their rows start on
+  // 16-byte boundaries (groups per row a multiple of 8, 16-byte aligned
+  // base); otherwise each dequantizing thread loads its own.
+  return pl.stma ? launch<BITS, TRANS, BN, true>(a, pl, stream, status)
+                 : launch<BITS, TRANS, BN, false>(a, pl, stream, status);
 }
 
 template <int BITS, bool TRANS>
-int launch_bn(const Args& a, cudaStream_t stream, int* status) {
-  const int64_t n_out = TRANS ? a.w_rows : a.w_cols;
-  const int64_t tiles_n = (n_out + kBM - 1) / kBM;
-  const int sms = sm_count();
-  // Largest token tile that still gives every SM a CTA (M-side padding is
-  // zero-filled by TMA and never stored).
-  int bn = 32;
-  // TQ_QMM_BN pins the token tile (256, 128, 64 or 32) for tuning runs.
-  static const int forced = [] {
-    const char* e = getenv("TQ_QMM_BN");
-    return e ? atoi(e) : 0;
-  }();
-  if (forced == 256 || forced == 128 || forced == 64 || forced == 32) {
-    bn = forced;
-  } else {
-  for (int cand : {256, 128, 64}) {
-    if (a.m >= cand / 2 && ((a.m + cand - 1) / cand) * tiles_n >= sms) {
-      bn = cand;
-      break;
-    }
-  }
-  if (bn == 32 && a.m > 32) bn = a.m > 128 ? 128 : 64;
-  }
-  switch (bn) {
-    case 256: return launch_scales<BITS, TRANS, 256>(a, stream, status);
-    case 128: return launch_scales<BITS, TRANS, 128>(a, stream, status);
-    case 64: return launch_scales<BITS, TRANS, 64>(a, stream, status);
-    default: return launch_scales<BITS, TRANS, 32>(a, stream, status);
+int launch_bn(const Args& a, const Plan& pl, cudaStream_t stream, int* status) {
+  switch (pl.bn) {
+    case 256: return launch_scales<BITS, TRANS, 256>(a, pl, stream, status);
+    case 128: return launch_scales<BITS, TRANS, 128>(a, pl, stream, status);
+    case 64: return launch_scales<BITS, TRANS, 64>(a, pl, stream, status);
+    default: return launch_scales<BITS, TRANS, 32>(a, pl, stream, status);
   }
 }
 
-int run(const Args& a, void* stream) {
+int validate(const Args& a) {
   if (a.bits != 4 && a.bits != 8) return fail(TQ_ERR_UNSUPPORTED, "bits must be 4 or 8, got %d", a.bits);
   if (a.group_size != 32 && a.group_size != 64 && a.group_size != 128)
     return fail(TQ_ERR_UNSUPPORTED, "group_size must be 32, 64 or 128, got %d", a.group_size);
@@ -709,20 +824,42 @@ int run(const Args& a, void* stream) {
   if (a.rank && (!a.lora_up || !a.lora_down))
     return fail(TQ_ERR_INVALID, "rank %d needs both lora_up and lora_down", a.rank);
   if (!a.transpose && a.bias) return fail(TQ_ERR_INVALID, "bias is only defined for transpose != 0");
-  if (a.m == 0 || a.w_rows == 0 || a.w_cols == 0) return TQ_OK;
+  return TQ_OK;
+}
+
+int validate_ptrs(const Args& a) {
+  if (a.m == 0 || a.w_rows == 0 || a.w_cols == 0) return TQ_OK;  // nothing is touched
   if (!a.x || !a.codes || !a.scales || !a.biases || !a.y) return fail(TQ_ERR_INVALID, "null pointer");
   if (!aligned(a.x, 16) || !aligned(a.codes, 16) || (a.rank && (!aligned(a.lora_up, 16) ||
                                                                  !aligned(a.lora_down, 16))))
     return fail(TQ_ERR_MISALIGNED, "x, codes, lora_up and lora_down must be 16-byte aligned");
   if (!aligned(a.y, 2) || !aligned(a.scales, 2) || !aligned(a.biases, 2))
     return fail(TQ_ERR_MISALIGNED, "y, scales and biases must be 2-byte aligned");
-  int rc = TQ_OK;
+  return TQ_OK;
+}
+
+int run(const Args& a, void* stream) {
+  int rc = validate(a);
+  if (rc) return rc;
+  rc = validate_ptrs(a);
+  if (rc) return rc;
+  if (a.m == 0 || a.w_rows == 0 || a.w_cols == 0) return TQ_OK;
+  // A workspace turns on split-K when the tiles alone cannot fill the GPU.
+  const Plan pl = make_plan(a, a.ws != nullptr);
+  if (pl.splits > 1) {
+    if (a.ws_bytes < pl.ws_bytes)
+      return fail(TQ_ERR_INVALID, "workspace of %zu bytes is smaller than the %zu this call needs",
+                  a.ws_bytes, pl.ws_bytes);
+    if (!aligned(a.ws, 16)) return fail(TQ_ERR_MISALIGNED, "workspace must be 16-byte aligned");
+    if (((a.transpose ? a.w_rows : a.w_cols) % 8) != 0)
+      return fail(TQ_ERR_INVALID, "split-K needs an output width that is a multiple of 8");
+  }
   int* status = device_status_ptr(&rc);
   if (!status) return rc;
   cudaStream_t s = as_stream(stream);
   if (a.bits == 4)
-    return a.transpose ? launch_bn<4, true>(a, s, status) : launch_bn<4, false>(a, s, status);
-  return a.transpose ? launch_bn<8, true>(a, s, status) : launch_bn<8, false>(a, s, status);
+    return a.transpose ? launch_bn<4, true>(a, pl, s, status) : launch_bn<4, false>(a, pl, s, status);
+  return a.transpose ? launch_bn<8, true>(a, pl, s, status) : launch_bn<8, false>(a, pl, s, status);
 }
 
 }  // namespace
@@ -744,5 +881,41 @@ extern "C" int tq_qlora_matmul(const void* x, const void* codes, const void* sca
   if (rank < 0 || rank > 16) return tq::fail(TQ_ERR_UNSUPPORTED, "LoRA rank must be 8 or 16");
   tq::Args a{x, codes, scales, biases, bias, lora_up, lora_down, m, w_rows, w_cols,
              transpose, group_size, bits, static_cast<int>(rank), y};
+  return tq::run(a, stream);
+}
+
+extern "C" int tq_qmm_workspace_bytes(int64_t m, int64_t w_rows, int64_t w_cols, int transpose,
+                                      int group_size, int bits, size_t* bytes) {
+  if (!bytes) return tq::fail(TQ_ERR_INVALID, "null output");
+  tq::Args a{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, m, w_rows, w_cols,
+             transpose, group_size, bits, 0, nullptr};
+  // Scales are taken as 16-byte aligned here (the caller's allocator's rule);
+  // a call whose scales are not falls back to no split and needs nothing.
+  a.scales = a.biases = reinterpret_cast<const void*>(static_cast<uintptr_t>(256));
+  int rc = tq::validate(a);
+  if (rc) return rc;
+  *bytes = (m == 0 || w_rows == 0 || w_cols == 0) ? 0 : tq::make_plan(a, true).ws_bytes;
+  return TQ_OK;
+}
+
+extern "C" int tq_quantized_matmul_ws(const void* x, const void* codes, const void* scales,
+                                      const void* biases, int64_t m, int64_t w_rows,
+                                      int64_t w_cols, int transpose, int group_size, int bits,
+                                      void* y, void* workspace, size_t workspace_bytes,
+                                      void* stream) {
+  tq::Args a{x, codes, scales, biases, nullptr, nullptr, nullptr, m, w_rows, w_cols,
+             transpose, group_size, bits, 0, y, workspace, workspace_bytes};
+  return tq::run(a, stream);
+}
+
+extern "C" int tq_qlora_matmul_ws(const void* x, const void* codes, const void* scales,
+                                  const void* biases, int64_t m, int64_t w_rows, int64_t w_cols,
+                                  int transpose, int group_size, int bits, const void* bias,
+                                  const void* lora_up, const void* lora_down, int64_t rank,
+                                  void* y, void* workspace, size_t workspace_bytes,
+                                  void* stream) {
+  if (rank < 0 || rank > 16) return tq::fail(TQ_ERR_UNSUPPORTED, "LoRA rank must be 8 or 16");
+  tq::Args a{x, codes, scales, biases, bias, lora_up, lora_down, m, w_rows, w_cols,
+             transpose, group_size, bits, static_cast<int>(rank), y, workspace, workspace_bytes};
   return tq::run(a, stream);
 }

@@ -184,6 +184,20 @@ def _gemm_operands(op, x, w_q, scales, biases, transpose, group_size, bits):
     return x2, w_rows, w_cols, n_out
 
 
+def _workspace(m: int, w_rows: int, w_cols: int, transpose: bool, group_size: int, bits: int,
+               device) -> tuple[torch.Tensor | None, int]:
+    """The split-K workspace a call needs (allocated here, by torch's caching
+    allocator; the library itself never allocates)."""
+    import ctypes
+
+    nbytes = ctypes.c_size_t(0)
+    check(lib().tq_qmm_workspace_bytes(m, w_rows, w_cols, 1 if transpose else 0, group_size,
+                                       bits, ctypes.byref(nbytes)))
+    if nbytes.value == 0:
+        return None, 0
+    return torch.empty(nbytes.value, dtype=torch.uint8, device=device), nbytes.value
+
+
 def quantized_matmul(x: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor,
                      biases: torch.Tensor, transpose: bool = True, group_size: int = 64,
                      bits: int = 4) -> torch.Tensor:
@@ -193,10 +207,12 @@ def quantized_matmul(x: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor,
                                                group_size, bits)
     y = torch.empty(tuple(x.shape[:-1]) + (n_out,), dtype=torch.bfloat16, device=x.device)
     with torch.cuda.device(x.device):
-        _launch("qmm", lambda: lib().tq_quantized_matmul(
+        ws, ws_bytes = _workspace(x2.shape[0], w_rows, w_cols, transpose, group_size, bits,
+                                  x.device)
+        _launch("qmm", lambda: lib().tq_quantized_matmul_ws(
             _ptr(x2), _ptr(w_q.contiguous()), _ptr(scales.contiguous()), _ptr(biases.contiguous()),
             x2.shape[0], w_rows, w_cols, 1 if transpose else 0, group_size, bits, _ptr(y),
-            _stream()), 2.0 * x2.shape[0] * w_rows * w_cols)
+            _ptr(ws), ws_bytes, _stream()), 2.0 * x2.shape[0] * w_rows * w_cols)
     return y
 
 
@@ -238,10 +254,13 @@ def qlora_matmul(x: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, biase
     down = lora_down.contiguous().reshape(-1, rank) if lora_down is not None else None
     b = bias.contiguous() if bias is not None else None
     with torch.cuda.device(x.device):
-        _launch("qmm", lambda: lib().tq_qlora_matmul(
+        ws, ws_bytes = _workspace(x2.shape[0], w_rows, w_cols, transpose, group_size, bits,
+                                  x.device)
+        _launch("qmm", lambda: lib().tq_qlora_matmul_ws(
             _ptr(x2), _ptr(w_q.contiguous()), _ptr(scales.contiguous()), _ptr(biases.contiguous()),
             x2.shape[0], w_rows, w_cols, 1 if transpose else 0, group_size, bits, _ptr(b), _ptr(up),
-            _ptr(down), rank, _ptr(y), _stream()), 2.0 * x2.shape[0] * w_rows * w_cols)
+            _ptr(down), rank, _ptr(y), _ptr(ws), ws_bytes, _stream()),
+            2.0 * x2.shape[0] * w_rows * w_cols)
     return y
 
 
