@@ -139,6 +139,29 @@ int tq_qlora_matmul_ws(const void* x, const void* codes, const void* scales, con
                        int64_t rank, void* y, void* workspace, size_t workspace_bytes,
                        void* stream);
 
+/*
+ * tq_quantized_matmul with no workspace argument and no allocation: the
+ * split-K partials live in a fixed 8 MiB array inside the library
+ * (TQ_NOALLOC_SCRATCH_BYTES; every GPU that loads the library holds it until
+ * the process exits).  For callers that cannot call cudaMalloc at call time:
+ * a runtime with no device allocator of its own, or one whose device memory
+ * is owned by a pool that this code may not draw from.
+ * - A shape whose split needs more than the array (tq_qmm_workspace_bytes >
+ *   TQ_NOALLOC_SCRATCH_BYTES) is refused with TQ_ERR_INVALID; every call of
+ *   up to 48 tokens fits, and most up to 128 (4096 x 4096 at 128 needs 6 MiB).
+ * - The first call on a device looks up the array's device address (once per
+ *   device, with that device current); make that first call before any
+ *   stream capture.
+ * - All calls on a device share the one array.  Nothing in it has to start
+ *   at zero (each call writes every partial it reads), but calls that
+ *   overlap on the GPU (different streams, no ordering between them) race.
+ * Results equal tq_quantized_matmul_ws's.  No counterpart in the reference.
+ */
+#define TQ_NOALLOC_SCRATCH_BYTES (8u << 20)
+int tq_quantized_matmul_noalloc(const void* x, const void* codes, const void* scales,
+                                const void* biases, int64_t m, int64_t w_rows, int64_t w_cols,
+                                int transpose, int group_size, int bits, void* y, void* stream);
+
 /* ------------------------------------------------------- LoRA side branch */
 
 /*

@@ -31,6 +31,7 @@
 #include <cuda_bf16.h>
 
 #include <cstdlib>
+#include <mutex>
 
 #include "tq_ptx.cuh"
 #include "tq_runtime.h"
@@ -918,4 +919,74 @@ extern "C" int tq_qlora_matmul_ws(const void* x, const void* codes, const void* 
   tq::Args a{x, codes, scales, biases, bias, lora_up, lora_down, m, w_rows, w_cols,
              transpose, group_size, bits, static_cast<int>(rank), y, workspace, workspace_bytes};
   return tq::run(a, stream);
+}
+
+// ------------------------------------------------- fixed-scratch variant ---
+//
+// tq_quantized_matmul_noalloc: the split-K GEMM with its f32 partials in a
+// file-scope device array instead of a caller workspace, for callers that
+// cannot allocate device memory at call time (an allocator-free runtime, a
+// host that has handed its whole memory budget to a pool it does not own).
+// The array is part of this module's image: every GPU that loads the library
+// holds its 8 MiB until the process exits.
+
+namespace tq {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = TQ_NOALLOC_SCRATCH_BYTES;
+
+// Split-K partials of tq_quantized_matmul_noalloc, shared by all its calls on
+// a device.  Host code must not pass this name to a kernel: on the host it is
+// only a stand-in; the device address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kScratchMaxDevices = 64;
+void* g_scratch_ptr[kScratchMaxDevices] = {};
+std::mutex g_scratch_mu;
+
+// The device address of the scratch array on the current device, resolved
+// once per device with that device current.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kScratchMaxDevices)
+    return fail(TQ_ERR_CUDA, "no current CUDA device");
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    const int rc = check_cuda(cudaGetSymbolAddress(&p, g_noalloc_scratch),
+                              "cudaGetSymbolAddress(split-K scratch)");
+    if (rc) return rc;
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return TQ_OK;
+}
+
+}  // namespace
+}  // namespace tq
+
+extern "C" int tq_quantized_matmul_noalloc(const void* x, const void* codes, const void* scales,
+                                           const void* biases, int64_t m, int64_t w_rows,
+                                           int64_t w_cols, int transpose, int group_size,
+                                           int bits, void* y, void* stream) {
+  using namespace tq;
+  Args a{x, codes, scales, biases, nullptr, nullptr, nullptr, m, w_rows, w_cols,
+         transpose, group_size, bits, 0, y};
+  int rc = validate(a);
+  if (rc) return rc;
+  rc = validate_ptrs(a);
+  if (rc) return rc;
+  if (m == 0 || w_rows == 0 || w_cols == 0) return TQ_OK;
+  const Plan pl = make_plan(a, true);
+  if (pl.ws_bytes > kNoAllocScratchBytes)
+    return fail(TQ_ERR_INVALID,
+                "tq_quantized_matmul_noalloc: this shape needs %zu bytes of split-K scratch, "
+                "more than the fixed %zu-byte array (use tq_quantized_matmul_ws)",
+                pl.ws_bytes, kNoAllocScratchBytes);
+  // Every partial the reduce reads is written by the GEMM of the same call
+  // first, so the array needs no clearing between calls.
+  rc = noalloc_scratch(&a.ws);
+  if (rc) return rc;
+  a.ws_bytes = kNoAllocScratchBytes;
+  return run(a, stream);
 }
