@@ -52,6 +52,9 @@ CASES = [
     (96, 1024, 2048, 8, 16.0, 8, 32, False),
     # small m: split-K (LoRA added by the first split only, bias by the reduce)
     (32, 1024, 2048, 16, 32.0, 4, 64, True),
+    # large: CTA pairs, token tile 128 then 256 both ways
+    (1536, 3072, 2560, 16, 32.0, 4, 64, True),
+    (2304, 4096, 2560, 8, 16.0, 8, 32, False),
 ]
 
 

@@ -32,6 +32,13 @@ CASES = [
     # small m: split-K over f32 partials in a workspace
     (16, 4096, 4096, 4, 64),
     (100, 2048, 2048, 8, 32),
+    # large: CTA pairs (cta_group::2) on 256-row weight tiles.  Forward token
+    # tile 128 and dX 256, m ragged; then a last tile whose second CTA lies
+    # wholly past the weight's rows; 8-bit both ways; both ways at 256.
+    (2000, 2304, 2560, 4, 64),
+    (1100, 3080, 1024, 8, 32),
+    (2048, 2560, 2048, 8, 64),
+    (4096, 4096, 4096, 4, 64),
 ]
 
 

@@ -234,6 +234,26 @@ __device__ __forceinline__ void dequant_tile(uint32_t cb, uint32_t ab, int t, ui
   }
 }
 
+// Scale-tile path: virtual dequantizing thread v (0..255) of one k-step reads
+// its group's scale and bias from the stage's 8-group tiles and dequantizes
+// its 32 codes.
+template <int BITS, bool TRANS>
+__device__ __forceinline__ void dequant_run(const Params& p, uint32_t sc, uint32_t bi, uint32_t cb,
+                                            uint32_t ab, int v, int out0, int k0) {
+  const GroupCoord gc = group_coord<TRANS>(p, v, out0, k0);
+  const uint32_t gx = static_cast<uint32_t>(scale_window<TRANS>(p, out0, k0));
+  const uint32_t row = TRANS ? static_cast<uint32_t>(v & 127) : static_cast<uint32_t>(v & 63);
+  const uint32_t off = row * 16 + (gc.g - gx) * 2;
+  const uint32_t s2 = bf16_dup(static_cast<uint16_t>(lds_u16(sc + off)));
+  const uint32_t b2 = bf16_dup(static_cast<uint16_t>(lds_u16(bi + off)));
+  dequant_tile<BITS, TRANS>(cb, ab, v, s2, b2);
+}
+
+// With scale tiles the dequantizing warps form two groups of four that take
+// alternate k-steps (two steps in flight); each thread covers virtual
+// threads tt and tt + 128.  The fallback path keeps all eight on every step.
+constexpr int kDqGroupWarps = kDqWarps / 2;
+
 // Persistent: CTA b takes tiles b, b + grid, ...; tile t covers output
 // features (t % tiles_n) * 128 and tokens (t / tiles_n) * BN.
 template <int BITS, bool TRANS, int BN, bool STMA>
@@ -312,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(empty_b(s), 1);
     }
     for (int a = 0; a < A; ++a) {
-      mbar_init(aready_b(a), kDqWarps);
+      mbar_init(aready_b(a), STMA ? kDqGroupWarps : kDqWarps);
       mbar_init(aempty_b(a), 1);
     }
     mbar_init(lora_full, 1);
@@ -466,15 +486,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int a = j % A;
       if (!mbar_wait(full_b(s), (j / S) & 1, p.status)) return false;
       if (!mbar_wait(aempty_b(a), ((j / A) & 1) ^ 1, p.status)) return false;
-      if constexpr (STMA) {
-        // This thread's scale and bias from the stage's 8-group tiles.
-        const GroupCoord gc = group_coord<TRANS>(p, t, out0, k0);
-        const uint32_t gx = static_cast<uint32_t>(scale_window<TRANS>(p, out0, k0));
-        const uint32_t row = TRANS ? static_cast<uint32_t>(t & 127) : static_cast<uint32_t>(t & 63);
-        const uint32_t off = row * 16 + (gc.g - gx) * 2;
-        s2 = bf16_dup(static_cast<uint16_t>(lds_u16(sc_s(s) + off)));
-        b2 = bf16_dup(static_cast<uint16_t>(lds_u16(bi_s(s) + off)));
-      }
       dequant_tile<BITS, TRANS>(c_s(s), a_s(a), t, s2, b2);
       fence_proxy_async_smem();
       __syncwarp();
@@ -482,11 +493,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       return true;
     };
     if constexpr (STMA) {
+      const int grp = t >> 7;
+      const int tt = t & 127;
       int j = 0;
       bool ok = true;
       for (int lt = 0; lt < my_tiles && ok; ++lt) {
         const int out0 = tile_out0(lt), kb = k_first(lt), kc = k_count(lt);
-        for (int kk = 0; kk < kc && ok; ++kk, ++j) ok = step(j, out0, (kb + kk) * kBK, 0u, 0u);
+        for (int kk = 0; kk < kc && ok; ++kk, ++j) {
+          if ((j & 1) != grp) continue;
+          const int s = j % S;
+          const int a = j % A;
+          const int k0 = (kb + kk) * kBK;
+          ok = mbar_wait(full_b(s), (j / S) & 1, p.status) &&
+               mbar_wait(aempty_b(a), ((j / A) & 1) ^ 1, p.status);
+          if (!ok) break;
+          dequant_run<BITS, TRANS>(p, sc_s(s), bi_s(s), c_s(s), a_s(a), tt, out0, k0);
+          dequant_run<BITS, TRANS>(p, sc_s(s), bi_s(s), c_s(s), a_s(a), tt + 128, out0, k0);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(aready_b(a));
+        }
       }
     } else {
       GroupRaw ring[kRing];
@@ -571,6 +597,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+}  // namespace
+}  // namespace tq
+
+#include "qmm_pair.cuh"
+
+namespace tq {
+namespace {
+
 struct Args {
   const void* x;
   const void* codes;
@@ -592,6 +626,7 @@ struct Args {
 struct Plan {
   int bn = 32;
   bool stma = false;
+  bool pair = false;  // two CTAs per 256-row tile (cta_group::2)
   int splits = 1;
   int k_steps_per_split = 1;
   size_t ws_bytes = 0;
@@ -640,6 +675,23 @@ Plan make_plan(const Args& a, bool allow_split) {
       }
     }
   }
+  // Large problems run on CTA pairs when there are enough 256-row tiles to
+  // give every pair one (TQ_QMM_PAIR=0 keeps single CTAs, for comparison).
+  static const bool pair_off = [] {
+    const char* e = getenv("TQ_QMM_PAIR");
+    return e && e[0] == '0';
+  }();
+  if (!pair_off && pl.stma && pl.splits == 1 && n_out > kBM) {
+    const int64_t pair_tiles_n = (n_out + 2 * kBM - 1) / (2 * kBM);
+    const int pairs = sm_count() / 2;
+    for (int cand : {256, 128}) {
+      if (a.m >= cand / 2 && ((a.m + cand - 1) / cand) * pair_tiles_n >= pairs) {
+        pl.pair = true;
+        pl.bn = cand;
+        break;
+      }
+    }
+  }
   return pl;
 }
 
@@ -679,17 +731,23 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
   }
 }
 
-template <int BITS, bool TRANS, int BN, bool STMA>
-int launch(const Args& a, const Plan& pl, cudaStream_t stream, int* status) {
-  using C = Cfg<BITS, TRANS, BN, STMA>;
+// The six tensor maps of one call.  x_rows: token rows per box (the token
+// tile, or its half for a CTA of a pair); sc_rows: weight rows per scale box.
+struct Maps {
+  CUtensorMap x, c, lup, ldn, sc, bi;
+};
+
+template <int BITS, bool TRANS>
+int make_maps(const Args& a, int x_rows, int sc_rows, bool stma, Maps& mp) {
   const int64_t k_red = TRANS ? a.w_cols : a.w_rows;
-  const int64_t n_out = TRANS ? a.w_rows : a.w_cols;
-  CUtensorMap tm_x, tm_c, tm_lup, tm_ldn, tm_sc, tm_bi;
+  CUtensorMap &tm_x = mp.x, &tm_c = mp.c, &tm_lup = mp.lup, &tm_ldn = mp.ldn, &tm_sc = mp.sc,
+              &tm_bi = mp.bi;
+  const int BN = x_rows;
   int rc;
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(k_red), static_cast<uint64_t>(a.m)};
     const uint64_t strides[1] = {static_cast<uint64_t>(k_red) * 2};
-    const uint32_t box[2] = {kBK, BN};
+    const uint32_t box[2] = {kBK, static_cast<uint32_t>(BN)};
     rc = encode_tmap(&tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.x, dims, strides, box,
                      CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
@@ -712,11 +770,11 @@ int launch(const Args& a, const Plan& pl, cudaStream_t stream, int* status) {
     rc = encode_tmap(&tm_c, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, a.codes, dims, strides, box, sw);
     if (rc) return rc;
   }
-  if constexpr (STMA) {
+  if (stma) {
     const uint64_t gpr = static_cast<uint64_t>(a.w_cols / a.group_size);
     const uint64_t dims[2] = {gpr, static_cast<uint64_t>(a.w_rows)};
     const uint64_t strides[1] = {gpr * 2};
-    const uint32_t box[2] = {8, static_cast<uint32_t>(C::SC_ROWS)};
+    const uint32_t box[2] = {8, static_cast<uint32_t>(sc_rows)};
     rc = encode_tmap(&tm_sc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.scales, dims, strides, box,
                      CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
@@ -744,7 +802,7 @@ int launch(const Args& a, const Plan& pl, cudaStream_t stream, int* status) {
     if (rc) return rc;
     const uint64_t dims[2] = {static_cast<uint64_t>(a.rank), static_cast<uint64_t>(a.m)};
     const uint64_t strides[1] = {static_cast<uint64_t>(a.rank) * 2};
-    const uint32_t box[2] = {8, BN};
+    const uint32_t box[2] = {8, static_cast<uint32_t>(BN)};
     rc = encode_tmap(&tm_ldn, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.lora_down, dims, strides, box,
                      CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
@@ -752,6 +810,12 @@ int launch(const Args& a, const Plan& pl, cudaStream_t stream, int* status) {
     tm_lup = tm_x;
     tm_ldn = tm_x;
   }
+  return TQ_OK;
+}
+
+Params make_params(const Args& a, const Plan& pl, int tile_rows, int bn, int* status) {
+  const int64_t k_red = a.transpose ? a.w_cols : a.w_rows;
+  const int64_t n_out = a.transpose ? a.w_rows : a.w_cols;
   Params p;
   p.scales = static_cast<const uint16_t*>(a.scales);
   p.biases = static_cast<const uint16_t*>(a.biases);
@@ -764,20 +828,31 @@ int launch(const Args& a, const Plan& pl, cudaStream_t stream, int* status) {
   p.groups_per_row = static_cast<int>(a.w_cols / a.group_size);
   p.group_shift = a.group_size == 32 ? 5 : (a.group_size == 64 ? 6 : 7);
   p.lora_rank = a.rank;
-  p.tiles_n = static_cast<int>((n_out + kBM - 1) / kBM);
-  const int64_t tiles_m = (a.m + BN - 1) / BN;
+  p.tiles_n = static_cast<int>((n_out + tile_rows - 1) / tile_rows);
+  const int64_t tiles_m = (a.m + bn - 1) / bn;
   p.tiles_total = static_cast<int>(p.tiles_n * tiles_m);
   p.splits = pl.splits;
   p.k_steps_per_split = pl.k_steps_per_split;
   p.ws = static_cast<float*>(a.ws);
   p.status = status;
+  return p;
+}
+
+template <int BITS, bool TRANS, int BN, bool STMA>
+int launch(const Args& a, const Plan& pl, cudaStream_t stream, int* status) {
+  using C = Cfg<BITS, TRANS, BN, STMA>;
+  const int64_t n_out = TRANS ? a.w_rows : a.w_cols;
+  Maps mp;
+  int rc = make_maps<BITS, TRANS>(a, BN, C::SC_ROWS, STMA, mp);
+  if (rc) return rc;
+  const Params p = make_params(a, pl, kBM, BN, status);
   auto kernel = qmm_kernel<BITS, TRANS, BN, STMA>;
   rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
                   "cudaFuncSetAttribute(qmm smem)");
   if (rc) return rc;
   const int units = p.tiles_total * p.splits;
   const int grid = units < sm_count() ? units : sm_count();
-  kernel<<<grid, kThreads, C::SMEM, stream>>>(tm_x, tm_c, tm_lup, tm_ldn, tm_sc, tm_bi, p);
+  kernel<<<grid, kThreads, C::SMEM, stream>>>(mp.x, mp.c, mp.lup, mp.ldn, mp.sc, mp.bi, p);
   rc = check_cuda(cudaGetLastError(), "qmm launch");
   if (rc || pl.splits == 1) return rc;
   const int64_t nv = a.m * n_out / 8;
@@ -798,8 +873,71 @@ int launch_scales(const Args& a, const Plan& pl, cudaStream_t stream, int* statu
                  : launch<BITS, TRANS, BN, false>(a, pl, stream, status);
 }
 
+// Pairs of CTAs the GPU holds at once for a pair kernel (cluster of 2, one
+// CTA per SM), per device; sm_count / 2 if the query fails.
+template <class K>
+int resident_pairs(K kernel, int smem) {
+  constexpr int kMaxDev = 64;
+  static int cache[kMaxDev] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return sm_count() / 2;
+  if (cache[dev] > 0) return cache[dev];
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(kernel), &cfg) !=
+          cudaSuccess ||
+      n <= 0) {
+    cudaGetLastError();
+    n = sm_count() / 2;
+  }
+  cache[dev] = n;
+  return n;
+}
+
+template <int BITS, bool TRANS, int BN>
+int launch_pair(const Args& a, const Plan& pl, cudaStream_t stream, int* status) {
+  using C = PairCfg<BITS, TRANS, BN>;
+  Maps mp;
+  int rc = make_maps<BITS, TRANS>(a, BN / 2, C::SC_ROWS, true, mp);
+  if (rc) return rc;
+  const Params p = make_params(a, pl, kPairRows, BN, status);
+  auto kernel = qmm_pair_kernel<BITS, TRANS, BN>;
+  rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
+                  "cudaFuncSetAttribute(qmm pair smem)");
+  if (rc) return rc;
+  const int pairs = resident_pairs(kernel, C::SMEM);
+  const int grid_pairs = p.tiles_total < pairs ? p.tiles_total : pairs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * grid_pairs, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(C::SMEM);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kernel, mp.x, mp.c, mp.lup, mp.ldn, mp.sc, mp.bi, p),
+                    "qmm pair launch");
+}
+
 template <int BITS, bool TRANS>
 int launch_bn(const Args& a, const Plan& pl, cudaStream_t stream, int* status) {
+  if (pl.pair)
+    return pl.bn == 256 ? launch_pair<BITS, TRANS, 256>(a, pl, stream, status)
+                        : launch_pair<BITS, TRANS, 128>(a, pl, stream, status);
   switch (pl.bn) {
     case 256: return launch_scales<BITS, TRANS, 256>(a, pl, stream, status);
     case 128: return launch_scales<BITS, TRANS, 128>(a, pl, stream, status);

@@ -249,6 +249,92 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N, bool a_mn, 
          (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// ------------------------------------------------------------- CTA pairs ---
+//
+// Two CTAs of a cluster that issue one tcgen05 MMA between them
+// (cta_group::2).  Barrier addresses that cross the pair are shared::cluster
+// addresses made with mapa; a CTA's own shared::cta addresses are used as is
+// for its own data.
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// The shared::cluster address of the same offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+// Every thread of both CTAs.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n"
+      "barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+
+// One arrival on an mbarrier of either CTA (cbar: shared::cluster address).
+// Default semantics (release at CTA scope), as for a local arrive: a
+// cluster-scope release here stalls the arriving warp on a memory barrier
+// every step.  Shared-memory data the arrival publishes to the tensor cores
+// is ordered by fence.proxy.async before it.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cbar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cbar) : "memory");
+}
+
+// TMA 2D load into this CTA's shared memory, completion counted on an
+// mbarrier of either CTA of the pair (cbar: shared::cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map,
+                                                 uint32_t cbar, int32_t c0, int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(cbar), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// TMEM allocation shared by the pair: one warp of each CTA (same warp id).
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// D (+)= A * B^T over the pair: M = 256 rows, 128 in each CTA's shared memory
+// and TMEM at the same offsets; B's N rows split in halves likewise.
+// Issued by one thread of the even CTA.
+__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                               uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n"
+      "}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive once on the mbarrier at cbar (either CTA) when every pair UMMA this
+// thread issued so far completes.
+__device__ __forceinline__ void umma_commit_pair(uint32_t cbar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cbar)
+      : "memory");
+}
+
 // ------------------------------------------------------- bf16x2 arithmetic --
 
 // Round-to-nearest-even a*b + c on packed bf16 pairs (single rounding).
