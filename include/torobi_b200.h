@@ -259,6 +259,31 @@ int tq_swiglu_fwd(const void* g, const void* u, int64_t n, void* a, void* stream
 int tq_swiglu_bwd(const void* g, const void* u, const void* da, int64_t n, void* dg, void* du,
                   void* stream);
 
+/* ----------------------------------------------------------------- loss --- */
+
+/*
+ * Cross-entropy per position, in f32, of bf16 logits [rows, vocab] (row
+ * pitch ld elements, ld >= vocab) against int64 targets [rows]:
+ *   lse[r]  = log(sum_j exp(z[r, j]))       (largest logit taken out first)
+ *   loss[r] = lse[r] - z[r, targets[r]]
+ * No reduction: which positions count, and how, is the caller's (as the
+ * reference's node: engine/src/interp.rs:434-444, config/ops.yml:212-220).
+ * A target outside [0, vocab) picks nothing (loss = lse).
+ */
+int tq_cross_entropy_fwd(const void* logits, const int64_t* targets, int64_t rows, int64_t vocab,
+                         int64_t ld, float* lse, float* loss, void* stream);
+
+/*
+ * Its VJP: dlogits[r, j] = RNE_bf16(scale * dloss[r] * (exp(z[r, j] - lse[r])
+ * - [j == targets[r]])), dlogits with row pitch ld; dloss may be NULL (all
+ * ones).  dlogits may be the logits buffer itself (each logit is read before
+ * its gradient overwrites it), so the backward needs no second
+ * [rows, vocab] buffer.
+ */
+int tq_cross_entropy_bwd(const void* logits, const int64_t* targets, const float* lse,
+                         int64_t rows, int64_t vocab, int64_t ld, const float* dloss, float scale,
+                         void* dlogits, void* stream);
+
 /* ------------------------------------------------------ data parallel ---- */
 /*
  * NCCL communicator for the data-parallel step (no reference counterpart:

@@ -305,6 +305,19 @@ def cross_entropy(logits, targets) -> np.ndarray:
     return (lse - picked).astype(np.float32)
 
 
+def cross_entropy_vjp(logits, targets, dloss) -> np.ndarray:
+    """VJP of ``cross_entropy`` wrt the logits, in f32: dloss[r] *
+    (softmax(logits[r]) - onehot(targets[r])), the gradient MLX derives for
+    logsumexp - take_along_axis (engine/src/interp.rs:440-444)."""
+    z = np.asarray(logits, np.float32)
+    mx = z.max(axis=-1, keepdims=True)
+    e = np.exp(z - mx)
+    p = e / np.sum(e, axis=-1, keepdims=True, dtype=np.float32)
+    t = np.asarray(targets)
+    p[np.arange(z.shape[0]), t] -= np.float32(1.0)
+    return (p * np.asarray(dloss, np.float32)[:, None]).astype(np.float32)
+
+
 # ------------------------------------------------------- seeded inputs -----
 
 def normal_bf16(rng: np.random.Generator, shape, std=1.0) -> np.ndarray:

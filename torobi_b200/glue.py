@@ -107,3 +107,42 @@ class _SwiGLU(torch.autograd.Function):
 def swiglu(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
     """(g * sigmoid(g)) * u."""
     return _SwiGLU.apply(g, u)
+
+
+class _CrossEntropy(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, z, targets, inplace):
+        _need_cuda("cross_entropy", z=z, targets=targets)
+        z = _bf16_contig("logits", z)
+        vocab = z.shape[-1]
+        rows = z.numel() // vocab if vocab else 0
+        t = targets.reshape(-1).to(torch.int64).contiguous()
+        if t.numel() != rows:
+            raise ValueError(f"targets hold {t.numel()} positions, logits {rows}")
+        lse = torch.empty(rows, dtype=torch.float32, device=z.device)
+        loss = torch.empty(rows, dtype=torch.float32, device=z.device)
+        _launch("cross_entropy", lambda: lib().tq_cross_entropy_fwd(
+            _ptr(z), _ptr(t), rows, vocab, vocab, _ptr(lse), _ptr(loss), _stream()))
+        ctx.save_for_backward(z, t, lse)
+        ctx.inplace = inplace
+        return loss.view(z.shape[:-1])
+
+    @staticmethod
+    def backward(ctx, dloss):
+        z, t, lse = ctx.saved_tensors
+        vocab = z.shape[-1]
+        rows = z.numel() // vocab
+        dl = dloss.reshape(-1).float().contiguous()
+        dz = z if ctx.inplace else torch.empty_like(z)
+        _launch("cross_entropy", lambda: lib().tq_cross_entropy_bwd(
+            _ptr(z), _ptr(t), _ptr(lse), rows, vocab, vocab, _ptr(dl), 1.0, _ptr(dz), _stream()))
+        return dz, None, None
+
+
+def cross_entropy(logits: torch.Tensor, targets: torch.Tensor,
+                  inplace: bool = False) -> torch.Tensor:
+    """Per-position ``logsumexp(logits) - logits[target]`` in f32 (no
+    reduction, as the reference's loss node), logits bf16 [..., vocab].
+    ``inplace=True`` writes the gradient over the logits in backward (no
+    second [rows, vocab] buffer); the graph then cannot be run backward twice."""
+    return _CrossEntropy.apply(logits, targets, inplace)

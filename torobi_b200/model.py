@@ -223,11 +223,13 @@ class QLoRACausalLM:
         return h @ head.t()
 
     def loss(self, ids: torch.Tensor) -> torch.Tensor:
-        """Mean next-token cross-entropy (f32) over positions 0..S-2."""
+        """Mean next-token cross-entropy (f32) over positions 0..S-2: the
+        fused per-position loss kernel, its gradient written over the bf16
+        logits in backward."""
         h = self.hidden(ids)[:, :-1]
-        z = self.logits(h).float()
+        z = self.logits(h)
         tgt = ids[:, 1:]
-        return F.cross_entropy(z.reshape(-1, z.shape[-1]), tgt.reshape(-1))
+        return glue.cross_entropy(z, tgt, inplace=True).mean()
 
     def base_nbytes(self) -> int:
         return sum(w.nbytes() for blk in self.blocks for w in blk.linears.values())
