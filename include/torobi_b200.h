@@ -147,8 +147,9 @@ int tq_qlora_matmul_ws(const void* x, const void* codes, const void* scales, con
  * a runtime with no device allocator of its own, or one whose device memory
  * is owned by a pool that this code may not draw from.
  * - A shape whose split needs more than the array (tq_qmm_workspace_bytes >
- *   TQ_NOALLOC_SCRATCH_BYTES) is refused with TQ_ERR_INVALID; every call of
- *   up to 48 tokens fits, and most up to 128 (4096 x 4096 at 128 needs 6 MiB).
+ *   TQ_NOALLOC_SCRATCH_BYTES) is refused with TQ_ERR_INVALID; on a 148-SM
+ *   B200 every call of up to 200 tokens fits (256 tokens x 1152 outputs
+ *   needs 9 MiB).
  * - The first call on a device looks up the array's device address (once per
  *   device, with that device current); make that first call before any
  *   stream capture.

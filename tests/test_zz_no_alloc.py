@@ -82,7 +82,7 @@ def test_noalloc_refuses_a_split_larger_than_the_array(cuda):
     from torobi_b200._lib import TQ_ERR_INVALID, lib
 
     L = lib()
-    m, n, k, tr, bits, group = 64, 18816, 4096, 1, 4, 64
+    m, n, k, tr, bits, group = 256, 1152, 4096, 1, 4, 64
     need = _workspace_bytes(L, m, n, k, tr, bits, group)
     if need <= LIMIT:
         pytest.skip(f"this GPU plans {need} bytes for the shape; nothing to refuse")

@@ -66,10 +66,16 @@ struct Cfg {
   static constexpr int LUP_BYTES = kBM * 16 * 2;            // [128 x 16] bf16
   static constexpr int LDN_BYTES = BN * 16 * 2;             // [BN x 16] bf16
   static constexpr int LORA_BYTES = ((LUP_BYTES + LDN_BYTES + 1023) / 1024) * 1024;
-  static constexpr int BAR_BYTES = 256;
+  static constexpr int BAR_BYTES = 512;
   static constexpr int FIXED = 1024 + LORA_BYTES + BAR_BYTES;
-  static constexpr int S3 = (kSmemLimit - FIXED - 3 * A_BYTES) / STAGE_BYTES;
-  static constexpr int A_BUFS = S3 >= 4 ? 3 : 2;
+  // Dequantizing groups on alternate k-steps: with scale tiles, two for the
+  // large token tiles (the MMA is long) and four for the small ones (the
+  // MMA is short and the dequantization's latency is the whole step); one
+  // dequantized-tile buffer more than groups.
+  static constexpr int DQ_GROUPS = !STMA ? 1 : (BN <= 64 ? 4 : 2);
+  static constexpr int A_WANT = DQ_GROUPS == 4 ? 5 : 3;
+  static constexpr int stages_with(int a) { return (kSmemLimit - FIXED - a * A_BYTES) / STAGE_BYTES; }
+  static constexpr int A_BUFS = stages_with(A_WANT) >= 4 ? A_WANT : (stages_with(3) >= 4 ? 3 : 2);
   static constexpr int STAGES_RAW = (kSmemLimit - FIXED - A_BUFS * A_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr int SMEM = FIXED + A_BUFS * A_BYTES + STAGES * STAGE_BYTES;
@@ -168,90 +174,119 @@ __device__ __forceinline__ uint32_t widen(uint32_t raw, uint32_t flag_from) {
 }
 
 // Packed codes (shared, as TMA left them) -> bf16 weight tile in the UMMA's
-// 128B-swizzled canonical layout.  t = dequantizing thread (0..255) owns 32
-// codes of one weight row; s2/b2 its group's bf16 scale/bias pair.
+// 128B-swizzled canonical layout.  Virtual dequantizing thread v (0..255) owns
+// 32 codes of one weight row: load_run fetches them (4 words at 4 bits, 8 at
+// 8), store_run dequantizes them with the group's bf16 scale/bias pair s2/b2
+// and writes them.  Split so that a thread can issue the loads of two runs
+// before the stores of either (the shared-memory accesses are ordered asm).
 template <int BITS, bool TRANS>
-__device__ __forceinline__ void dequant_tile(uint32_t cb, uint32_t ab, int t, uint32_t s2,
-                                             uint32_t b2) {
+__device__ __forceinline__ void load_run(uint32_t cb, int v, uint32_t (&w)[BITS]) {
   if constexpr (TRANS) {
-    // K-major: row r = output feature, k half hh; chunks 4hh..4hh+3 of the
-    // row's eight 16-byte chunks.
-    const int r = t & 127;
-    const int hh = t >> 7;
+    // K-major: row r = output feature, k half hh.
+    const int r = v & 127;
+    const int hh = v >> 7;
     if constexpr (BITS == 4) {
-      uint32_t w[4];
       lds128(cb + swz<32>(r * 32 + hh * 16), w[0], w[1], w[2], w[3]);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t o[4];
-        dequant_u4x8(w[j], s2, b2, o);
-        sts128(ab + r * 128 + (((4 * hh + j) ^ (r & 7)) << 4), o[0], o[1], o[2], o[3]);
-      }
     } else {
-      uint32_t w[8];
 #pragma unroll
       for (int c = 0; c < 2; ++c)
         lds128(cb + swz<64>(r * 64 + (2 * hh + c) * 16), w[4 * c], w[4 * c + 1], w[4 * c + 2],
                w[4 * c + 3]);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t o0[2], o1[2];
-        dequant_u8x4(w[2 * j], s2, b2, o0);
-        dequant_u8x4(w[2 * j + 1], s2, b2, o1);
-        sts128(ab + r * 128 + (((4 * hh + j) ^ (r & 7)) << 4), o0[0], o0[1], o1[0], o1[1]);
-      }
     }
   } else {
-    // MN-major: kr = reduction row (0..63), qq = output quarter (32 outputs);
-    // atoms of 64 outputs x 8 reduction rows, 8 K-groups per 64-output block.
-    const int kr = t & 63;
-    const int qq = t >> 6;
-    const uint32_t row_off = (qq >> 1) * 8192 + (kr >> 3) * 1024 + (kr & 7) * 128;
-    const int j0 = (qq & 1) * 4;  // first 16-byte chunk within the 64-output atom row
+    // MN-major: kr = reduction row (0..63), qq = output quarter (32 outputs).
+    const int kr = v & 63;
+    const int qq = v >> 6;
     if constexpr (BITS == 4) {
-      uint32_t w[4];
       lds128(cb + swz<64>(kr * 64 + qq * 16), w[0], w[1], w[2], w[3]);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t o[4];
-        dequant_u4x8(w[j], s2, b2, o);
-        sts128(ab + row_off + (((j0 + j) ^ (kr & 7)) << 4), o[0], o[1], o[2], o[3]);
-      }
     } else {
-      uint32_t w[8];
 #pragma unroll
       for (int c = 0; c < 2; ++c)
         lds128(cb + swz<128>(kr * 128 + (2 * qq + c) * 16), w[4 * c], w[4 * c + 1],
                w[4 * c + 2], w[4 * c + 3]);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t o0[2], o1[2];
-        dequant_u8x4(w[2 * j], s2, b2, o0);
-        dequant_u8x4(w[2 * j + 1], s2, b2, o1);
-        sts128(ab + row_off + (((j0 + j) ^ (kr & 7)) << 4), o0[0], o0[1], o1[0], o1[1]);
-      }
     }
   }
 }
 
-// Scale-tile path: virtual dequantizing thread v (0..255) of one k-step reads
-// its group's scale and bias from the stage's 8-group tiles and dequantizes
-// its 32 codes.
 template <int BITS, bool TRANS>
-__device__ __forceinline__ void dequant_run(const Params& p, uint32_t sc, uint32_t bi, uint32_t cb,
-                                            uint32_t ab, int v, int out0, int k0) {
+__device__ __forceinline__ void store_run(uint32_t ab, int v, const uint32_t (&w)[BITS],
+                                          uint32_t s2, uint32_t b2) {
+  uint32_t base;
+  int j0, sw;
+  if constexpr (TRANS) {
+    // Chunks 4hh..4hh+3 of row r's eight 16-byte chunks.
+    const int r = v & 127;
+    base = ab + r * 128;
+    j0 = 4 * (v >> 7);
+    sw = r & 7;
+  } else {
+    // Atoms of 64 outputs x 8 reduction rows, 8 K-groups per 64-output block.
+    const int kr = v & 63;
+    const int qq = v >> 6;
+    base = ab + (qq >> 1) * 8192 + (kr >> 3) * 1024 + (kr & 7) * 128;
+    j0 = (qq & 1) * 4;
+    sw = kr & 7;
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t o[4];
+    if constexpr (BITS == 4) {
+      dequant_u4x8(w[j], s2, b2, o);
+    } else {
+      uint32_t lo[2], hi[2];
+      dequant_u8x4(w[2 * j], s2, b2, lo);
+      dequant_u8x4(w[2 * j + 1], s2, b2, hi);
+      o[0] = lo[0];
+      o[1] = lo[1];
+      o[2] = hi[0];
+      o[3] = hi[1];
+    }
+    sts128(base + (((j0 + j) ^ sw) << 4), o[0], o[1], o[2], o[3]);
+  }
+}
+
+template <int BITS, bool TRANS>
+__device__ __forceinline__ void dequant_tile(uint32_t cb, uint32_t ab, int t, uint32_t s2,
+                                             uint32_t b2) {
+  uint32_t w[BITS];
+  load_run<BITS, TRANS>(cb, t, w);
+  store_run<BITS, TRANS>(ab, t, w, s2, b2);
+}
+
+// Byte offset of virtual thread v's group scale (and bias) in the stage's
+// 8-group scale tile.
+template <bool TRANS>
+__device__ __forceinline__ uint32_t scale_off(const Params& p, int v, int out0, int k0) {
   const GroupCoord gc = group_coord<TRANS>(p, v, out0, k0);
   const uint32_t gx = static_cast<uint32_t>(scale_window<TRANS>(p, out0, k0));
   const uint32_t row = TRANS ? static_cast<uint32_t>(v & 127) : static_cast<uint32_t>(v & 63);
-  const uint32_t off = row * 16 + (gc.g - gx) * 2;
-  const uint32_t s2 = bf16_dup(static_cast<uint16_t>(lds_u16(sc + off)));
-  const uint32_t b2 = bf16_dup(static_cast<uint16_t>(lds_u16(bi + off)));
-  dequant_tile<BITS, TRANS>(cb, ab, v, s2, b2);
+  return row * 16 + (gc.g - gx) * 2;
 }
 
-// With scale tiles the dequantizing warps form two groups of four that take
-// alternate k-steps (two steps in flight); each thread covers virtual
-// threads tt and tt + 128.  The fallback path keeps all eight on every step.
+// Scale-tile path: one thread of a group of 256/G dequantizes virtual
+// threads tt + i * 256/G (i < G) of a k-step, every load issued before the
+// first store.
+template <int BITS, bool TRANS, int G>
+__device__ __forceinline__ void dequant_runs(const Params& p, uint32_t sc, uint32_t bi,
+                                             uint32_t cb, uint32_t ab, int tt, int out0, int k0) {
+  constexpr int kStride = 256 / G;
+  uint32_t off[G], w[G][BITS], sv[G], bv[G];
+#pragma unroll
+  for (int i = 0; i < G; ++i) off[i] = scale_off<TRANS>(p, tt + i * kStride, out0, k0);
+#pragma unroll
+  for (int i = 0; i < G; ++i) load_run<BITS, TRANS>(cb, tt + i * kStride, w[i]);
+#pragma unroll
+  for (int i = 0; i < G; ++i) {
+    sv[i] = lds_u16(sc + off[i]);
+    bv[i] = lds_u16(bi + off[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < G; ++i)
+    store_run<BITS, TRANS>(ab, tt + i * kStride, w[i], bf16_dup(static_cast<uint16_t>(sv[i])),
+                           bf16_dup(static_cast<uint16_t>(bv[i])));
+}
+
+// Warps per dequantizing group of the pair kernel (two groups of four).
 constexpr int kDqGroupWarps = kDqWarps / 2;
 
 // Persistent: CTA b takes tiles b, b + grid, ...; tile t covers output
@@ -332,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(empty_b(s), 1);
     }
     for (int a = 0; a < A; ++a) {
-      mbar_init(aready_b(a), STMA ? kDqGroupWarps : kDqWarps);
+      mbar_init(aready_b(a), kDqWarps / C::DQ_GROUPS);
       mbar_init(aempty_b(a), 1);
     }
     mbar_init(lora_full, 1);
@@ -493,22 +528,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       return true;
     };
     if constexpr (STMA) {
-      const int grp = t >> 7;
-      const int tt = t & 127;
+      constexpr int G = C::DQ_GROUPS;
+      const int grp = t / (256 / G);
+      const int tt = t % (256 / G);
       int j = 0;
       bool ok = true;
       for (int lt = 0; lt < my_tiles && ok; ++lt) {
         const int out0 = tile_out0(lt), kb = k_first(lt), kc = k_count(lt);
         for (int kk = 0; kk < kc && ok; ++kk, ++j) {
-          if ((j & 1) != grp) continue;
+          if ((j % G) != grp) continue;
           const int s = j % S;
           const int a = j % A;
           const int k0 = (kb + kk) * kBK;
           ok = mbar_wait(full_b(s), (j / S) & 1, p.status) &&
                mbar_wait(aempty_b(a), ((j / A) & 1) ^ 1, p.status);
           if (!ok) break;
-          dequant_run<BITS, TRANS>(p, sc_s(s), bi_s(s), c_s(s), a_s(a), tt, out0, k0);
-          dequant_run<BITS, TRANS>(p, sc_s(s), bi_s(s), c_s(s), a_s(a), tt + 128, out0, k0);
+          dequant_runs<BITS, TRANS, G>(p, sc_s(s), bi_s(s), c_s(s), a_s(a), tt, out0, k0);
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) mbar_arrive(aready_b(a));
@@ -632,14 +667,19 @@ struct Plan {
   size_t ws_bytes = 0;
 };
 
-int pick_bn(int64_t m, int64_t n_out) {
-  const int64_t tiles_n = (n_out + kBM - 1) / kBM;
-  const int sms = sm_count();
-  // TQ_QMM_BN pins the token tile (256, 128, 64 or 32) for tuning runs.
+// TQ_QMM_BN pins the token tile (256, 128, 64 or 32) for tuning runs.
+int forced_bn() {
   static const int forced = [] {
     const char* e = getenv("TQ_QMM_BN");
     return e ? atoi(e) : 0;
   }();
+  return forced;
+}
+
+int pick_bn(int64_t m, int64_t n_out) {
+  const int64_t tiles_n = (n_out + kBM - 1) / kBM;
+  const int sms = sm_count();
+  const int forced = forced_bn();
   if (forced == 256 || forced == 128 || forced == 64 || forced == 32) return forced;
   // Largest token tile that still gives every SM a tile (M-side padding is
   // zero-filled by TMA and never stored).
@@ -664,7 +704,8 @@ Plan make_plan(const Args& a, bool allow_split) {
     const int64_t tiles = ((n_out + kBM - 1) / kBM) * ((a.m + pl.bn - 1) / pl.bn);
     const int sms = sm_count();
     if (tiles < sms && num_k >= 8) {
-      int splits = static_cast<int>((sms + tiles - 1) / tiles);
+      // As many splits as keep every unit in one wave over the SMs.
+      int splits = static_cast<int>(sms / tiles);
       const int max_splits = num_k / 4 < 16 ? num_k / 4 : 16;  // >= 4 k-steps per split
       if (splits > max_splits) splits = max_splits;
       if (splits > 1) {
@@ -684,7 +725,9 @@ Plan make_plan(const Args& a, bool allow_split) {
   if (!pair_off && pl.stma && pl.splits == 1 && n_out > kBM) {
     const int64_t pair_tiles_n = (n_out + 2 * kBM - 1) / (2 * kBM);
     const int pairs = sm_count() / 2;
+    const int forced = forced_bn();
     for (int cand : {256, 128}) {
+      if ((forced == 256 || forced == 128) && cand != forced) continue;
       if (a.m >= cand / 2 && ((a.m + cand - 1) / cand) * pair_tiles_n >= pairs) {
         pl.pair = true;
         pl.bn = cand;

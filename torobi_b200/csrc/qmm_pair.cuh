@@ -298,8 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = mbar_wait(full_b(s), (j / S) & 1, p.status) &&
              mbar_wait(aempty_b(a), ((j / A) & 1) ^ 1, p.status);
         if (!ok) break;
-        dequant_run<BITS, TRANS>(p, sc_s(s), bi_s(s), c_s(s), a_s(a), tt, out0, k0);
-        dequant_run<BITS, TRANS>(p, sc_s(s), bi_s(s), c_s(s), a_s(a), tt + 128, out0, k0);
+        dequant_runs<BITS, TRANS, 2>(p, sc_s(s), bi_s(s), c_s(s), a_s(a), tt, out0, k0);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(lead(aready_b(a)));
