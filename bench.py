@@ -19,8 +19,10 @@ events around each launch on its stream, against the measured sustained bf16
 tensor peak.  ``cpu_baseline``: the CPU oracle on a bounded sample.
 
 Kernel workloads (one GPU): ``--workload qmm`` (one quantized_matmul shape),
-``qmm-sweep`` (M x projection shapes, forward and dX) and ``quant-sweep``
-(quantize/dequantize over every Qwen2.5-0.5B-shaped linear).
+``qmm-sweep`` (M x projection shapes, forward and dX), ``quant-sweep``
+(quantize/dequantize over every Qwen2.5-0.5B-shaped linear), ``merge`` (the
+export merge over a Llama-3-8B-shaped layer) and ``load`` (quantize-at-load
+of a published bf16 file).
 """
 from __future__ import annotations
 
@@ -48,7 +50,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--workload", choices=("llama3-8b", "qwen2.5-0.5b", "qmm", "qmm-sweep",
-                                          "quant-sweep"), default="llama3-8b")
+                                          "quant-sweep", "merge", "load"), default="llama3-8b")
     p.add_argument("--m", type=int, default=16384, help="qmm: tokens")
     p.add_argument("--n", type=int, default=4096, help="qmm: weight rows (out features)")
     p.add_argument("--k", type=int, default=4096, help="qmm: weight cols (in features)")
@@ -519,6 +521,83 @@ def run_kernels(args):
                                        "peak_kind": f"{peak_kind} copy"},
                           "sweep": rows}), flush=True)
         return 0
+    if args.workload == "merge":
+        # The export merge over one Llama-3-8B-shaped layer's seven linears
+        # (4-bit g64, LoRA r16): reads bits/8 + 4/g bytes of packed weight
+        # and writes 4 bytes of f32 per element.
+        from torobi_b200 import ops
+        from torobi_b200.model import LLAMA3_8B
+
+        g = torch.Generator(device=dev)
+        g.manual_seed(0)
+        r = LLAMA3_8B.lora_rank
+        total_ms = 0.0
+        nbytes = 0.0
+        rows = []
+        for name, (o, i) in LLAMA3_8B.linear_shapes().items():
+            c, s_, b_ = ops.quantize((torch.randn(o, i, device=dev, generator=g) * 0.02)
+                                     .bfloat16(), 64, 4)
+            a = torch.randn(r, i, device=dev, generator=g) * 0.01
+            bb = torch.randn(o, r, device=dev, generator=g) * 0.01
+            ms = _time_kernel(lambda: ops.lora_merge(c, s_, b_, 64, 4, lora_a=a, lora_b=bb,
+                                                     scale=2.0), K, W, flush)
+            nb = o * i * (0.5 + 4 / 64 + 4)
+            rows.append({"linear": name, "rows": o, "cols": i, "ms": ms, "gbs": nb / ms / 1e6})
+            total_ms += ms
+            nbytes += nb
+        val = nbytes / total_ms / 1e6
+        print(json.dumps({"metric": "LoRA merge for export GB/s (Llama-3-8B layer, r16)",
+                          "value": val, "unit": "GB/s", "scaling": "weak", "dtype": "u4 -> f32",
+                          **common,
+                          "config": {"workload": "dequantize + scale * B A, f32 out",
+                                     "l2": "flushed before every launch"},
+                          "roofline": {"bound": "hbm", "achieved": val, "peak": hbm,
+                                       "unit": "GB/s", "frac": val / hbm,
+                                       "peak_kind": f"{peak_kind} copy"},
+                          "linears": rows}), flush=True)
+        return 0
+    if args.workload == "load":
+        # Quantize-at-load of a published dense bf16 file (Llama-3-8B shapes,
+        # --layers deep, default 2): file -> host -> device -> quantized.
+        import dataclasses
+        import shutil
+
+        from torobi_b200.model import LLAMA3_8B, QLoRACausalLM
+        from torobi_b200.weights import published_parameters, write_dense
+
+        cfg = dataclasses.replace(LLAMA3_8B, layers=args.layers or 2)
+        tmp = Path(tempfile.mkdtemp(prefix="tq_load_"))
+        try:
+            gcpu = torch.Generator().manual_seed(0)
+            dense = {d.path: (torch.randn(d.shape, generator=gcpu) * 0.02).bfloat16()
+                     for d in published_parameters(cfg)}
+            f = tmp / "model.safetensors"
+            write_dense(f, dense, metadata={"format": "pt"})
+            lin = sum(t.numel() * 2 for k, t in dense.items() if k.endswith("_proj.weight"))
+            total = sum(t.numel() * 2 for t in dense.values())
+            del dense
+            times = []
+            for it in range(W + K):
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                m = QLoRACausalLM.from_pretrained(cfg, f, device=dev)
+                torch.cuda.synchronize()
+                if it >= W:
+                    times.append(time.perf_counter() - t0)
+                del m
+            sec = sorted(times)[len(times) // 2]
+        finally:
+            shutil.rmtree(tmp, ignore_errors=True)
+        print(json.dumps({"metric": "quantize-at-load GB/s (published bf16 file to a QLoRA model)",
+                          "value": total / sec / 1e9, "unit": "GB/s", "scaling": "weak",
+                          "dtype": "bf16 -> u4", **common, "ms_per_step": sec * 1e3,
+                          "config": {"workload": "from_pretrained, Llama-3-8B shapes",
+                                     "layers": cfg.layers, "file_bytes": total,
+                                     "linear_bytes": lin,
+                                     "linear_gbs": lin / sec / 1e9,
+                                     "timing": "wall clock, file in the page cache"}}),
+              flush=True)
+        return 0
     raise SystemExit(f"unknown kernel workload {args.workload}")
 
 
@@ -526,7 +605,7 @@ def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference(args)
-    if args.workload in ("qmm", "qmm-sweep", "quant-sweep"):
+    if args.workload in ("qmm", "qmm-sweep", "quant-sweep", "merge", "load"):
         return run_kernels(args)
     return run_ours(args)
 

@@ -260,6 +260,25 @@ int tq_swiglu_fwd(const void* g, const void* u, int64_t n, void* a, void* stream
 int tq_swiglu_bwd(const void* g, const void* u, const void* da, int64_t n, void* dg, void* du,
                   void* stream);
 
+/* --------------------------------------------------------------- export --- */
+
+/*
+ * A quantized linear merged with its LoRA pair, for export:
+ *   out[r, c] = deq(r, c) + scale * sum_i lora_b[r, i] * lora_a[i, c]
+ * deq = RNE_bf16(scale_g * q + bias_g) as the GEMM uses it; the low-rank sum
+ * in f32, i ascending, each product and sum rounded on its own, then scaled
+ * and added (so a CPU restatement matches bit for bit).  lora_a f32
+ * [rank, cols], lora_b f32 [rows, rank]; rank 0 with both NULL
+ * gives the dequantized weight.  out [rows, cols] f32 (out_dtype
+ * TQ_DTYPE_F32) or bf16 (TQ_DTYPE_BF16, rounded once).  The merge the
+ * reference's export asks for and does not have (lib/torobi/export.rb:118-140;
+ * its export writes f32, engine/src/export.rs:1-9).
+ */
+int tq_lora_merge(const void* codes, const void* scales, const void* biases, int64_t rows,
+                  int64_t cols, int group_size, int bits, const float* lora_a,
+                  const float* lora_b, int64_t rank, float scale, void* out, int out_dtype,
+                  void* stream);
+
 /* ----------------------------------------------------------------- loss --- */
 
 /*

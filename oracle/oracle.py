@@ -305,6 +305,22 @@ def cross_entropy(logits, targets) -> np.ndarray:
     return (lse - picked).astype(np.float32)
 
 
+def lora_merge(codes, scales, biases, bits, group, a=None, b=None, scale=1.0) -> np.ndarray:
+    """f32 [rows, cols] = dequantize(W) + scale * (b @ a), the sum over the
+    rank taken in increasing order with every product and sum rounded to f32
+    on its own: the merge an adapted linear's export needs (the reference's
+    ``W + scale * BA``, lib/torobi/export.rb:118-127)."""
+    deq = f32_from_bf16(dequantize(codes, scales, biases, bits, group))
+    if a is None:
+        return (deq + np.float32(scale) * np.zeros_like(deq)).astype(np.float32)
+    a = np.asarray(a, np.float32)
+    b = np.asarray(b, np.float32)
+    acc = np.zeros(deq.shape, np.float32)
+    for i in range(a.shape[0]):
+        acc = acc + b[:, i:i + 1] * a[i:i + 1, :]
+    return (deq + np.float32(scale) * acc).astype(np.float32)
+
+
 def cross_entropy_vjp(logits, targets, dloss) -> np.ndarray:
     """VJP of ``cross_entropy`` wrt the logits, in f32: dloss[r] *
     (softmax(logits[r]) - onehot(targets[r])), the gradient MLX derives for

@@ -76,6 +76,8 @@ SIGNATURES = {
     "tq_rope": ([_vp, _i64, _i64, _i64, _i64, _vp, _vp, _i32, _vp, _vp], _i32),
     "tq_swiglu_fwd": ([_vp, _vp, _i64, _vp, _vp], _i32),
     "tq_swiglu_bwd": ([_vp, _vp, _vp, _i64, _vp, _vp, _vp], _i32),
+    "tq_lora_merge": ([_vp, _vp, _vp, _i64, _i64, _i32, _i32, _vp, _vp, _i64, _f32, _vp, _i32,
+                       _vp], _i32),
     "tq_cross_entropy_fwd": ([_vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp], _i32),
     "tq_cross_entropy_bwd": ([_vp, _vp, _vp, _i64, _i64, _i64, _vp, _f32, _vp, _vp], _i32),
     "tq_dp_unique_id": ([_vp], _i32),

@@ -29,6 +29,7 @@ import torch.nn.functional as F
 
 from . import glue
 from .qlora import Adapter, LoRAStore, QuantizedWeight, qlora_linear
+from .weights import linear_path
 
 LINEARS = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
 
@@ -136,51 +137,81 @@ class Block:
 
 
 class QLoRACausalLM:
-    """Random-init model with quantized block linears and a LoRA store."""
+    """A causal LM with quantized block linears and a LoRA store: random init,
+    or (``source``) a published model's weights quantized as they load."""
 
     def __init__(self, cfg: DecoderConfig, device: torch.device | str = "cuda", seed: int = 0,
-                 dtype: torch.dtype = torch.bfloat16):
+                 dtype: torch.dtype = torch.bfloat16, source=None):
         self.cfg = cfg
         self.device = torch.device(device)
         self.dtype = dtype
         gen = torch.Generator(device=self.device)
         gen.manual_seed(seed)
         dev = self.device
+
+        def take(path, shape, init):
+            # A published tensor by its path, shape-checked and converted to
+            # the compute dtype; or the random initialisation.
+            if source is None:
+                return init()
+            return source.tensor(path, shape, dtype, dev)
+
         # Embedding table: normal std 0.02 (lib/torobi/dsl/layers.rb:30-35).
-        self.embed = (torch.randn(cfg.vocab, cfg.hidden, device=dev, generator=gen) * 0.02).to(dtype)
-        self.final_norm = torch.ones(cfg.hidden, dtype=dtype, device=dev)
+        self.embed = take("model.embed_tokens.weight", (cfg.vocab, cfg.hidden),
+                          lambda: (torch.randn(cfg.vocab, cfg.hidden, device=dev,
+                                               generator=gen) * 0.02).to(dtype))
+        self.final_norm = take("model.norm.weight", (cfg.hidden,),
+                               lambda: torch.ones(cfg.hidden, dtype=dtype, device=dev))
         if cfg.tie_embeddings:
             self.lm_head = None
         else:
             bound = math.sqrt(6.0 / cfg.hidden)
-            self.lm_head = torch.empty(cfg.vocab, cfg.hidden, device=dev).uniform_(
-                -bound, bound, generator=gen).to(dtype)
+            self.lm_head = take("lm_head.weight", (cfg.vocab, cfg.hidden),
+                                lambda: torch.empty(cfg.vocab, cfg.hidden, device=dev).uniform_(
+                                    -bound, bound, generator=gen).to(dtype))
         self.store = LoRAStore(dev)
         shapes = cfg.linear_shapes()
         self.blocks: list[Block] = []
         for li in range(cfg.layers):
-            blk = Block(torch.ones(cfg.hidden, dtype=dtype, device=dev),
-                        torch.ones(cfg.hidden, dtype=dtype, device=dev))
+            pre = f"model.layers.{li}"
+            ones = lambda: torch.ones(cfg.hidden, dtype=dtype, device=dev)  # noqa: E731
+            blk = Block(take(f"{pre}.input_layernorm.weight", (cfg.hidden,), ones),
+                        take(f"{pre}.post_attention_layernorm.weight", (cfg.hidden,), ones))
             for name, (d_out, d_in) in shapes.items():
+                path = linear_path(li, name)
                 # Linear weights: kaiming_uniform, bound sqrt(6 / d_in)
-                # (engine/src/init.rs:42-55), quantized once at materialisation.
+                # (engine/src/init.rs:42-55), quantized once at materialisation
+                # (at load for a published model).
                 bound = math.sqrt(6.0 / d_in)
-                w = torch.empty(d_out, d_in, device=dev).uniform_(-bound, bound, generator=gen)
+                w = take(f"{path}.weight", (d_out, d_in),
+                         lambda: torch.empty(d_out, d_in, device=dev).uniform_(
+                             -bound, bound, generator=gen).to(dtype))
                 bias = None
                 if cfg.attention_bias and name in ("q_proj", "k_proj", "v_proj"):
-                    bias = torch.zeros(d_out, dtype=dtype, device=dev)
-                blk.linears[name] = QuantizedWeight.from_dense(w.to(dtype), cfg.bits, cfg.group,
-                                                               bias)
+                    bias = take(f"{path}.bias", (d_out,),
+                                lambda: torch.zeros(d_out, dtype=dtype, device=dev))
+                blk.linears[name] = QuantizedWeight.from_dense(w, cfg.bits, cfg.group, bias)
                 del w
                 if name in cfg.lora_targets:
                     self.store.declare(f"layers.{li}.{name}", d_in, d_out, cfg.lora_rank,
                                        cfg.lora_alpha)
             self.blocks.append(blk)
+        # The adapter's matrices are fresh whatever the source (they are in
+        # no published model): A drawn from the seed, B zero.
         self.store.materialize(gen)
         for li, blk in enumerate(self.blocks):
             for name in shapes:
                 blk.adapters[name] = self.store.adapters.get(f"layers.{li}.{name}")
         self._rope_cache: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
+
+    @classmethod
+    def from_pretrained(cls, cfg: DecoderConfig, path, device: torch.device | str = "cuda",
+                        seed: int = 0) -> "QLoRACausalLM":
+        """A published model's safetensors file, every block linear quantized
+        on the device as it arrives; the adapter fresh from ``seed``."""
+        from .weights import SafetensorsSource
+
+        return cls(cfg, device=device, seed=seed, source=SafetensorsSource(path))
 
     def _rope(self, seq: int):
         t = self._rope_cache.get(seq)

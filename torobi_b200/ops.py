@@ -14,7 +14,7 @@ from __future__ import annotations
 
 import torch
 
-from ._lib import check, lib
+from ._lib import TQ_DTYPE_BF16, TQ_DTYPE_F32, check, lib
 
 SUPPORTED_BITS = (4, 8)
 SUPPORTED_GROUPS = (32, 64, 128)
@@ -160,6 +160,44 @@ def dequantize(w_q: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
         _launch("dequantize", lambda: lib().tq_dequantize(
             _ptr(w_q.contiguous()), _ptr(scales.contiguous()), _ptr(biases.contiguous()), rows,
             cols, group_size, bits, _ptr(out), _stream()))
+    return out
+
+
+def lora_merge(w_q: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+               group_size: int = 64, bits: int = 4, lora_a: torch.Tensor | None = None,
+               lora_b: torch.Tensor | None = None, scale: float = 1.0,
+               dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """[rows, cols] = dequantize(W) + scale * lora_b @ lora_a (f32 sum, each op
+    rounded alone), in f32 or bf16: a quantized linear with its LoRA pair
+    merged, for export.  lora_a f32 [r, cols], lora_b f32 [rows, r]; neither
+    gives the dequantized weight."""
+    op = "lora_merge"
+    _need_cuda(op, w_q=w_q, scales=scales, biases=biases, lora_a=lora_a, lora_b=lora_b)
+    _check_bits_group(op, group_size, bits)
+    if w_q.dim() != 2:
+        raise ValueError(f"[{op}] the packed weight must be 2-D, got shape {tuple(w_q.shape)}")
+    cols = _check_packed(op, w_q, scales, biases, group_size, bits)
+    rows = w_q.shape[0]
+    if (lora_a is None) != (lora_b is None):
+        raise ValueError(f"[{op}] lora_a and lora_b come together")
+    rank = 0
+    if lora_a is not None:
+        if lora_a.dtype != torch.float32 or lora_b.dtype != torch.float32:
+            raise ValueError(f"[{op}] the LoRA factors must be float32")
+        rank = lora_a.shape[0]
+        if tuple(lora_a.shape) != (rank, cols) or tuple(lora_b.shape) != (rows, rank):
+            raise ValueError(f"[{op}] lora_a {tuple(lora_a.shape)} and lora_b "
+                             f"{tuple(lora_b.shape)} do not fit [{rows}, {cols}]")
+        lora_a, lora_b = lora_a.contiguous(), lora_b.contiguous()
+    if dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError(f"[{op}] dtype must be float32 or bfloat16")
+    out = torch.empty(rows, cols, dtype=dtype, device=w_q.device)
+    code = TQ_DTYPE_F32 if dtype == torch.float32 else TQ_DTYPE_BF16
+    with torch.cuda.device(w_q.device):
+        _launch("lora_merge", lambda: lib().tq_lora_merge(
+            _ptr(w_q.contiguous()), _ptr(scales.contiguous()), _ptr(biases.contiguous()), rows,
+            cols, group_size, bits, _ptr(lora_a), _ptr(lora_b), rank, float(scale), _ptr(out),
+            code, _stream()))
     return out
 
 
