@@ -14,9 +14,9 @@
 //               of the token tile and its LoRA tiles (the even CTA's barrier)
 //   warp 1      TMEM allocation in both CTAs; in the even CTA the thread that
 //               issues the pair UMMAs and commits to both CTAs' barriers
-//   warps 2-9   dequantize this CTA's 128 weight rows (two groups of four
-//               on alternate k-steps), then arrive on the even CTA's "weight
-//               tile ready" barrier
+//   warps 2-9   dequantize this CTA's 128 weight rows (G groups on
+//               alternate k-steps: 2 forward, 4 for dX), then arrive on the
+//               even CTA's "weight tile ready" barrier
 //   warps 10-13 epilogue: this CTA's 128 rows of the accumulator (its TMEM)
 // Barriers only the even CTA waits on (token tile full, weight tile ready,
 // LoRA full, accumulator drained) count both CTAs' arrivals; barriers each
@@ -29,7 +29,7 @@ namespace {
 
 constexpr int kPairRows = 2 * kBM;  // weight-side rows of a pair tile
 
-template <int BITS, bool TRANS, int BN>
+template <int BITS, bool TRANS, int BN, int G>
 struct PairCfg {
   static constexpr int XH_ROWS = BN / 2;                    // this CTA's tokens
   static constexpr int XH_BYTES = XH_ROWS * kBK * 2;
@@ -43,8 +43,10 @@ struct PairCfg {
   static constexpr int LORA_BYTES = ((LUP_BYTES + LDN_BYTES + 1023) / 1024) * 1024;
   static constexpr int BAR_BYTES = 512;
   static constexpr int FIXED = 1024 + LORA_BYTES + BAR_BYTES;
-  static constexpr int S3 = (kSmemLimit - FIXED - 3 * A_BYTES) / STAGE_BYTES;
-  static constexpr int A_BUFS = S3 >= 4 ? 3 : 2;
+  // G dequantizing groups on alternate k-steps, one weight-tile buffer more.
+  static constexpr int DQ_GROUPS = G;
+  static constexpr int stages_with(int a) { return (kSmemLimit - FIXED - a * A_BYTES) / STAGE_BYTES; }
+  static constexpr int A_BUFS = stages_with(G + 1) >= 4 ? G + 1 : (stages_with(3) >= 4 ? 3 : 2);
   static constexpr int STAGES_RAW = (kSmemLimit - FIXED - A_BUFS * A_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr int SMEM = FIXED + A_BUFS * A_BYTES + STAGES * STAGE_BYTES;
@@ -61,7 +63,7 @@ struct PairCfg {
 // tile t covers weight-side rows (t % tiles_n) * 256 (CTA rank r owns the
 // 128 rows from + 128 r) and tokens (t / tiles_n) * BN (CTA r loads the half
 // from + r * BN / 2).  p.tiles_n counts 256-row tiles; no split-K.
-template <int BITS, bool TRANS, int BN>
+template <int BITS, bool TRANS, int BN, int G>
 __global__ void __launch_bounds__(kThreads, 1)
     qmm_pair_kernel(const __grid_constant__ CUtensorMap tm_x,
                     const __grid_constant__ CUtensorMap tm_c,
@@ -69,7 +71,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __grid_constant__ CUtensorMap tm_ldn,
                     const __grid_constant__ CUtensorMap tm_sc,
                     const __grid_constant__ CUtensorMap tm_bi, const Params p) {
-  using C = PairCfg<BITS, TRANS, BN>;
+  using C = PairCfg<BITS, TRANS, BN, G>;
   constexpr int S = C::STAGES;
   constexpr int A = C::A_BUFS;
   extern __shared__ uint8_t smem_raw[];
@@ -133,7 +135,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(empty_b(s), 1);
     }
     for (int a = 0; a < A; ++a) {
-      mbar_init(aready_b(a), 2 * kDqGroupWarps);
+      mbar_init(aready_b(a), 2 * (kDqWarps / G));
       mbar_init(aempty_b(a), 1);
     }
     mbar_init(lora_full, 1);
@@ -282,23 +284,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp < 2 + kDqWarps) {
     // ---------------------------------------------------- dequant warps
-    // Two groups of four warps on alternate k-steps, as the single-CTA kernel.
+    // G groups of 8/G warps on alternate k-steps, as the single-CTA kernel.
     const int t = threadIdx.x - 64;  // 0..255
-    const int grp = t >> 7;
-    const int tt = t & 127;
+    const int grp = t / (256 / G);
+    const int tt = t % (256 / G);
     int j = 0;
     bool ok = true;
     for (int lt = 0; lt < my_tiles && ok; ++lt) {
       const int out0 = tile_out0(lt);
       for (int kk = 0; kk < num_k && ok; ++kk, ++j) {
-        if ((j & 1) != grp) continue;
+        if ((j % G) != grp) continue;
         const int s = j % S;
         const int a = j % A;
         const int k0 = kk * kBK;
         ok = mbar_wait(full_b(s), (j / S) & 1, p.status) &&
              mbar_wait(aempty_b(a), ((j / A) & 1) ^ 1, p.status);
         if (!ok) break;
-        dequant_runs<BITS, TRANS, 2>(p, sc_s(s), bi_s(s), c_s(s), a_s(a), tt, out0, k0);
+        dequant_runs<BITS, TRANS, G>(p, sc_s(s), bi_s(s), c_s(s), a_s(a), tt, out0, k0);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(lead(aready_b(a)));
