@@ -149,3 +149,28 @@ def test_zero_b_starts_as_the_base_model_and_training_moves_only_the_adapter(cud
     assert losses[-1] < losses[0] - 0.05, losses
     base_after = [w.codes for blk in model.blocks for w in blk.linears.values()]
     assert all(torch.equal(a, b) for a, b in zip(base_before, base_after))
+
+
+@pytest.mark.gpu
+def test_graph_replayed_steps_match_eager_steps(cuda):
+    """Trainer(graph=True) replays the forward/backward as a CUDA graph: the
+    same losses and parameters as eager steps (to the atomics' summation
+    order of the LoRA gradients), a new batch shape captured on its own."""
+    import torch
+
+    from torobi_b200.model import QLoRACausalLM, tiny_config
+    from torobi_b200.train import AdamWConfig, Trainer
+
+    cfg = tiny_config()
+    g = torch.Generator(device=cuda).manual_seed(4)
+    batches = [torch.randint(0, cfg.vocab, (4, 32), device=cuda, generator=g) for _ in range(3)]
+    runs = []
+    for graph in (False, True):
+        model = QLoRACausalLM(cfg, device=cuda, seed=11)
+        tr = Trainer(model, AdamWConfig(lr=1e-3), micro_batch=2, graph=graph)
+        losses = [float(tr.step(b)) for b in batches]
+        losses.append(float(tr.step(batches[0][:2])))  # another shape
+        runs.append((losses, model.store.params.clone()))
+    (l0, p0), (l1, p1) = runs
+    assert all(abs(a - b) <= 1e-5 * abs(a) for a, b in zip(l0, l1)), (l0, l1)
+    assert torch.allclose(p0, p1, rtol=0, atol=1e-5)

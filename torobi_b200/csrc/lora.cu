@@ -179,15 +179,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Opt in to the large dynamic shared memory (per device, so on every call).
+// Opt in to the large dynamic shared memory (once per device).
 int set_smem_once() {
-  int rc = check_cuda(cudaFuncSetAttribute(skinny_kernel<false>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem),
-                      "cudaFuncSetAttribute(skinny)");
+  int rc = set_max_smem_once(reinterpret_cast<const void*>(skinny_kernel<false>), kSmem,
+                             "cudaFuncSetAttribute(skinny)");
   if (rc) return rc;
-  return check_cuda(cudaFuncSetAttribute(skinny_kernel<true>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem),
-                    "cudaFuncSetAttribute(skinny)");
+  return set_max_smem_once(reinterpret_cast<const void*>(skinny_kernel<true>), kSmem,
+                           "cudaFuncSetAttribute(skinny)");
 }
 
 }  // namespace

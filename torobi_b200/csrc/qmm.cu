@@ -888,8 +888,8 @@ int launch(const Args& a, const Plan& pl, cudaStream_t stream, int* status) {
   if (rc) return rc;
   const Params p = make_params(a, pl, kBM, BN, status);
   auto kernel = qmm_kernel<BITS, TRANS, BN, STMA>;
-  rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
-                  "cudaFuncSetAttribute(qmm smem)");
+  rc = set_max_smem_once(reinterpret_cast<const void*>(kernel), C::SMEM,
+                         "cudaFuncSetAttribute(qmm smem)");
   if (rc) return rc;
   const int units = p.tiles_total * p.splits;
   const int grid = units < sm_count() ? units : sm_count();
@@ -953,8 +953,8 @@ int launch_pair(const Args& a, const Plan& pl, cudaStream_t stream, int* status)
   if (rc) return rc;
   const Params p = make_params(a, pl, kPairRows, BN, status);
   auto kernel = qmm_pair_kernel<BITS, TRANS, BN, G>;
-  rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
-                  "cudaFuncSetAttribute(qmm pair smem)");
+  rc = set_max_smem_once(reinterpret_cast<const void*>(kernel), C::SMEM,
+                         "cudaFuncSetAttribute(qmm pair smem)");
   if (rc) return rc;
   const int pairs = resident_pairs(kernel, C::SMEM);
   const int grid_pairs = p.tiles_total < pairs ? p.tiles_total : pairs;

@@ -60,6 +60,25 @@ int* device_status_ptr(int* err_code) {
   return g_status_ptr[dev];
 }
 
+int set_max_smem_once(const void* func, int bytes, const char* what) {
+  struct Entry {
+    const void* func;
+    int dev;
+  };
+  static Entry done[512];
+  static int n_done = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(TQ_ERR_CUDA, "no current CUDA device");
+  std::lock_guard<std::mutex> lock(g_mu);
+  for (int i = 0; i < n_done; ++i)
+    if (done[i].func == func && done[i].dev == dev) return TQ_OK;
+  const int rc = check_cuda(
+      cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), what);
+  if (rc) return rc;
+  if (n_done < 512) done[n_done++] = Entry{func, dev};
+  return TQ_OK;
+}
+
 int sm_count() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;

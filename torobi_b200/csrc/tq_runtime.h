@@ -37,4 +37,9 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
+// Raises a kernel's dynamic shared-memory limit on the current device, once
+// per (kernel, device): later calls return at once, so a launch inside a
+// stream capture makes no attribute call.
+int set_max_smem_once(const void* func, int bytes, const char* what);
+
 }  // namespace tq

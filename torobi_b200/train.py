@@ -105,8 +105,16 @@ class Trainer:
     """Runs QLoRA steps of a ``QLoRACausalLM`` on this rank's shard."""
 
     def __init__(self, model, opt: AdamWConfig | None = None, micro_batch: int = 1,
-                 reduce: NcclGradReduce | None = None, rank: int = 0, world: int = 1):
+                 reduce: NcclGradReduce | None = None, rank: int = 0, world: int = 1,
+                 graph: bool = False):
         self.model = model
+        # graph=True replays the forward and backward of every micro-batch as
+        # one CUDA graph (captured on the first step of a batch shape); the
+        # collective and the optimizer stay outside it (AdamW takes the step
+        # count from the host).  For small models, whose step the host's
+        # per-launch work would otherwise bound.
+        self.graph = graph
+        self._graphs: dict[tuple, tuple] = {}
         self.opt = opt or AdamWConfig()
         self.micro = micro_batch
         self.rank, self.world = rank, world
@@ -119,17 +127,47 @@ class Trainer:
         self.last_norm = float("nan")
         self._pending: list[float] = []  # grad scales of launched, unsettled steps
 
+    def _gradients(self, ids: torch.Tensor) -> None:
+        """Zeroes the gradient and loss buffers, then accumulates every
+        micro-batch's loss and adapter gradients into them."""
+        self.store.zero_grad()
+        self.loss_buf.zero_()
+        for a, b in micro_batches(ids.shape[0], self.micro):
+            loss = self.model.loss(ids[a:b])
+            loss.backward()
+            self.loss_buf += loss.detach()
+
+    def _graphed(self, ids: torch.Tensor):
+        key = (tuple(ids.shape), ids.dtype)
+        hit = self._graphs.get(key)
+        if hit is None:
+            static = ids.clone()
+            # Warm up on a side stream first (first-call set-up, allocator
+            # pools), as capture requires, then capture one pass.
+            side = torch.cuda.Stream(device=ids.device)
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                for _ in range(2):
+                    self._gradients(static)
+            torch.cuda.current_stream().wait_stream(side)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, capture_error_mode="thread_local"):
+                self._gradients(static)
+            hit = (g, static)
+            self._graphs[key] = hit
+        return hit
+
     def step(self, ids: torch.Tensor) -> torch.Tensor:
         """One optimizer step over this rank's rows ``ids`` [rows, seq] (on
         the device).  Returns the global mean loss as a device tensor."""
         st = self.store
-        st.zero_grad()
         parts = micro_batches(ids.shape[0], self.micro)
-        self.loss_buf.zero_()
-        for a, b in parts:
-            loss = self.model.loss(ids[a:b])
-            loss.backward()
-            self.loss_buf += loss.detach()
+        if self.graph:
+            g, static = self._graphed(ids)
+            static.copy_(ids)
+            g.replay()
+        else:
+            self._gradients(ids)
         self.reduce(st.grads)
         self.reduce(self.loss_buf)
         self.loss_buf /= float(self.world * len(parts))
