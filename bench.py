@@ -42,6 +42,12 @@ if str(ROOT) not in sys.path:
 METRIC = "QLoRA train tokens/s at 1/2/4/8 B200; int4 qmatmul TFLOP/s and % of roofline"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
+# DRAM bytes (read + write) per quantized-GEMM launch of the step, from one
+# ncu capture of the 2-layer step (dram__bytes_read.sum + dram__bytes_write.sum
+# over the timed step's 200 launches, per shape), weighted to the 32-layer
+# step's launch mix; profiles/llama3_8b_step_qmm_traffic.md.
+QMM_TRAFFIC_PER_LAUNCH = {"llama3-8b": 224.14e6}
+
 
 def parse_args():
     p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
@@ -307,7 +313,7 @@ def run_ours(args):
     trainer.settle()
     tokens_per_step = gb * seq
     value = tokens_per_step * K / (ms / 1000.0)
-    summ = rec.summary().get("qmm", {"launches": 0, "ms": 0.0, "flops": 0.0})
+    summ = rec.summary().get("qmm", {"launches": 0, "ms": 0.0, "flops": 0.0, "bytes": 0.0})
     launches = rec.launches()
     step_ms_for_share = local_ms
     roofline_timing = "every launch of the timed steps, CUDA events on its stream"
@@ -328,7 +334,7 @@ def run_ours(args):
         ops.set_recorder(None)
         trainer.settle()
         trainer.graph = True
-        summ = rec.summary().get("qmm", {"launches": 0, "ms": 0.0, "flops": 0.0})
+        summ = rec.summary().get("qmm", {"launches": 0, "ms": 0.0, "flops": 0.0, "bytes": 0.0})
         launches = rec.launches() * K
         step_ms_for_share = e0.elapsed_time(e1)
         roofline_timing = ("every launch of one eager step after the timed region (the timed "
@@ -360,7 +366,10 @@ def run_ours(args):
     peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
     roofline = {
         "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-        "frac": achieved / peak if peak else None, "traffic": None,
+        "frac": achieved / peak if peak else None,
+        "traffic": QMM_TRAFFIC_PER_LAUNCH.get(args.workload) if not args.layers else None,
+        "traffic_unit": "bytes per launch (ncu, DRAM read + write)",
+        "algorithmic_bytes_per_launch": summ.get("bytes", 0.0) / max(1, summ["launches"]),
         "kernel": "qmm_kernel (tcgen05 quantized_matmul, forward and dX, fused LoRA)",
         "peak_kind": f"{peak_kind} sustained bf16 (cuBLAS, long loop)",
         "launches_timed": int(summ["launches"]),

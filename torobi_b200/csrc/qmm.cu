@@ -389,6 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ producer
     if (elect_one_sync()) {
       tma_prefetch_desc(&tm_x);
+      const uint64_t keep = l2_evict_last();  // codes and scales: reused by every token tile
       tma_prefetch_desc(&tm_c);
       if constexpr (STMA) {
         tma_prefetch_desc(&tm_sc);
@@ -430,14 +431,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(full_b(s), C::X_BYTES + C::C_BYTES + 2 * C::SC_BYTES);
           tma_load_2d(x_s(s), &tm_x, full_b(s), k0, m0);
           if constexpr (TRANS)
-            tma_load_2d(c_s(s), &tm_c, full_b(s), k0 * BITS / 32, out0);
+            tma_load_2d_hint(c_s(s), &tm_c, full_b(s), k0 * BITS / 32, out0, keep);
           else
-            tma_load_2d(c_s(s), &tm_c, full_b(s), out0 * BITS / 32, k0);
+            tma_load_2d_hint(c_s(s), &tm_c, full_b(s), out0 * BITS / 32, k0, keep);
           if constexpr (STMA) {
             const int gx = scale_window<TRANS>(p, out0, k0);
             const int gy = TRANS ? out0 : k0;
-            tma_load_2d(sc_s(s), &tm_sc, full_b(s), gx, gy);
-            tma_load_2d(bi_s(s), &tm_bi, full_b(s), gx, gy);
+            tma_load_2d_hint(sc_s(s), &tm_sc, full_b(s), gx, gy, keep);
+            tma_load_2d_hint(bi_s(s), &tm_bi, full_b(s), gx, gy, keep);
           }
         }
       }

@@ -23,23 +23,25 @@ SUPPORTED_GROUPS = (32, 64, 128)
 class LaunchRecorder:
     """Counts this library's kernel launches and, for the kinds listed in
     ``timed``, brackets each launch with CUDA events on the launching stream
-    and accumulates the launch's algorithmic FLOPs (for the roofline)."""
+    and accumulates the launch's algorithmic FLOPs and bytes (for the
+    roofline)."""
 
     def __init__(self, timed=("qmm",)):
         self.timed = set(timed)
         self.counts: dict[str, int] = {}
-        self.pairs: list[tuple[str, torch.cuda.Event, torch.cuda.Event, float]] = []
+        self.pairs: list[tuple[str, torch.cuda.Event, torch.cuda.Event, float, float]] = []
 
     def launches(self) -> int:
         return sum(self.counts.values())
 
     def summary(self) -> dict[str, dict[str, float]]:
         out: dict[str, dict[str, float]] = {}
-        for kind, s, e, flops in self.pairs:
-            d = out.setdefault(kind, {"launches": 0, "ms": 0.0, "flops": 0.0})
+        for kind, s, e, flops, nbytes in self.pairs:
+            d = out.setdefault(kind, {"launches": 0, "ms": 0.0, "flops": 0.0, "bytes": 0.0})
             d["launches"] += 1
             d["ms"] += s.elapsed_time(e)
             d["flops"] += flops
+            d["bytes"] += nbytes
         return out
 
 
@@ -51,7 +53,7 @@ def set_recorder(rec: LaunchRecorder | None) -> None:
     _REC = rec
 
 
-def _launch(kind: str, call, flops: float = 0.0) -> None:
+def _launch(kind: str, call, flops: float = 0.0, nbytes: float = 0.0) -> None:
     rec = _REC
     if rec is None:
         check(call())
@@ -63,7 +65,7 @@ def _launch(kind: str, call, flops: float = 0.0) -> None:
         s.record()
         check(call())
         e.record()
-        rec.pairs.append((kind, s, e, flops))
+        rec.pairs.append((kind, s, e, flops, nbytes))
     else:
         check(call())
 
@@ -201,6 +203,13 @@ def lora_merge(w_q: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
     return out
 
 
+def _qmm_bytes(m, w_rows, w_cols, transpose, group_size, bits) -> float:
+    """Algorithmic bytes of one quantized GEMM: the activation read, the
+    packed weight with its scales and biases read, the output written."""
+    k_in, n_out = (w_cols, w_rows) if transpose else (w_rows, w_cols)
+    return 2.0 * m * k_in + w_rows * w_cols * (bits / 8 + 4 / group_size) + 2.0 * m * n_out
+
+
 def _gemm_operands(op, x, w_q, scales, biases, transpose, group_size, bits):
     _need_cuda(op, x=x, w_q=w_q, scales=scales, biases=biases)
     _check_bits_group(op, group_size, bits)
@@ -250,7 +259,8 @@ def quantized_matmul(x: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor,
         _launch("qmm", lambda: lib().tq_quantized_matmul_ws(
             _ptr(x2), _ptr(w_q.contiguous()), _ptr(scales.contiguous()), _ptr(biases.contiguous()),
             x2.shape[0], w_rows, w_cols, 1 if transpose else 0, group_size, bits, _ptr(y),
-            _ptr(ws), ws_bytes, _stream()), 2.0 * x2.shape[0] * w_rows * w_cols)
+            _ptr(ws), ws_bytes, _stream()), 2.0 * x2.shape[0] * w_rows * w_cols,
+            _qmm_bytes(x2.shape[0], w_rows, w_cols, transpose, group_size, bits))
     return y
 
 
@@ -298,7 +308,8 @@ def qlora_matmul(x: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, biase
             _ptr(x2), _ptr(w_q.contiguous()), _ptr(scales.contiguous()), _ptr(biases.contiguous()),
             x2.shape[0], w_rows, w_cols, 1 if transpose else 0, group_size, bits, _ptr(b), _ptr(up),
             _ptr(down), rank, _ptr(y), _ptr(ws), ws_bytes, _stream()),
-            2.0 * x2.shape[0] * w_rows * w_cols)
+            2.0 * x2.shape[0] * w_rows * w_cols,
+            _qmm_bytes(x2.shape[0], w_rows, w_cols, transpose, group_size, bits))
     return y
 
 
