@@ -55,7 +55,12 @@ struct PairCfg {
   static_assert(BN == 128 || BN == 256, "pair tiles span 128 or 256 tokens");
   static_assert(STAGES >= 2, "shared memory too small for two stages");
   static_assert(SMEM <= kSmemLimit, "shared memory budget");
-  static_assert(8 * (3 * STAGES + 2 * A_BUFS + 6) + 8 <= BAR_BYTES, "barrier area");
+  // Barrier area: stage (full, xfull, empty), weight ring (ready, empty),
+  // LoRA (full, empty), accumulators (full x2, empty x2), then the TMEM
+  // address word.
+  static constexpr int OFF_LORA = 8 * (3 * STAGES + 2 * A_BUFS);
+  static constexpr int OFF_TMEM = OFF_LORA + 48;
+  static_assert(OFF_TMEM + 4 <= BAR_BYTES, "barrier area");
   static_assert(STAGE_BYTES % 1024 == 0, "stage tiles stay 1024-byte aligned");
 };
 
@@ -95,11 +100,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto empty_b = [&](int s) { return bars + 8u * (2 * S + s); };   // own stage free
   auto aready_b = [&](int a) { return bars + 8u * (3 * S + a); };  // even CTA: both weight halves
   auto aempty_b = [&](int a) { return bars + 8u * (3 * S + A + a); };
-  const uint32_t lora_full = bars + 8u * (3 * S + 2 * A);          // even CTA: both CTAs' tiles
+  const uint32_t lora_full = bars + C::OFF_LORA;                   // even CTA: both CTAs' tiles
   const uint32_t lora_empty = lora_full + 8u;
   auto acc_full = [&](int b) { return lora_full + 16u + 8u * b; };
   auto acc_empty = [&](int b) { return lora_full + 32u + 8u * b; };  // even CTA: both epilogues
-  const uint32_t tmem_slot = lora_full + 48u;
+  const uint32_t tmem_slot = bars + C::OFF_TMEM;
   volatile uint32_t* tmem_slot_ptr =
       reinterpret_cast<volatile uint32_t*>(gbase + (tmem_slot - base));
 
