@@ -73,6 +73,33 @@ def test_quantize_edge_values_bit_exact(cuda, oracle, bits, group):
     _check_quantize(tq, oracle, _edge_matrix(oracle, 256), bits, group, cuda)
 
 
+def _half_integer_matrix(oracle, bits, cols, rng):
+    """Rows whose quotients (w - bias) / scale sit on or next to half-integers:
+    the cases where rounding the quotient to f32 decides the code, which the
+    kernel resolves with an IEEE division instead of its reciprocal product."""
+    f = np.float32
+    n = (1 << bits) - 1
+    rows = []
+    k = np.arange(cols, dtype=f) % (2 * n + 1) / f(2.0)         # 0, 0.5, ..., n: scale 1
+    rows.append(k)
+    rows.append(-k)
+    for c in rng.uniform(0.01, 3.0, size=14).astype(f):
+        r = (np.arange(cols, dtype=f) % n + f(0.5)) * c          # (j + 1/2) * c, bf16-rounded
+        r[0], r[1] = f(0.0), f(n) * c                             # pin the group range
+        rows.append(r)
+    return oracle.bf16_from_f32(np.stack(rows))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("group", [32, 64, 128])
+def test_quantize_half_integer_quotients_bit_exact(cuda, oracle, bits, group):
+    import torobi_b200 as tq
+
+    rng = np.random.default_rng(60 + bits + group)
+    _check_quantize(tq, oracle, _half_integer_matrix(oracle, bits, 512, rng), bits, group, cuda)
+
+
 @pytest.mark.gpu
 def test_quantize_ragged_and_tiny_shapes(cuda, oracle):
     import torobi_b200 as tq

@@ -26,78 +26,109 @@ __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
   return static_cast<uint16_t>((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
 }
 
-// One thread = 8 consecutive elements (one 16-byte vector).  LANES = lanes per
-// group = group_size / 8.
+// Quantizes one 16-byte vector (8 consecutive elements) held by lane `lane`
+// of a warp whose 32 lanes hold 32 consecutive vectors (vi its index).
+// LANES = lanes per group = group_size / 8; a group's min/max is reduced
+// across its lanes with shuffles, so every lane of the warp must call this.
+template <int BITS, int LANES>
+__device__ __forceinline__ void quantize_vector(uint4 raw, bool live, int64_t vi, int lane,
+                                                uint32_t* __restrict__ codes,
+                                                uint16_t* __restrict__ scales,
+                                                uint16_t* __restrict__ biases) {
+  constexpr float n_bins = static_cast<float>((1 << BITS) - 1);
+  constexpr float eps = 1e-7f;
+  const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+  float v[8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    v[2 * j] = bf16_bits_to_f32(words[j] & 0xFFFFu);
+    v[2 * j + 1] = bf16_bits_to_f32(words[j] >> 16);
+  }
+  float w_max = -INFINITY, w_min = INFINITY;
+  if (live) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      w_max = mlx_max(w_max, v[j]);
+      w_min = mlx_min(w_min, v[j]);
+    }
+  }
+#pragma unroll
+  for (int off = 1; off < LANES; off <<= 1) {
+    w_max = mlx_max(w_max, __shfl_xor_sync(0xffffffffu, w_max, off));
+    w_min = mlx_min(w_min, __shfl_xor_sync(0xffffffffu, w_min, off));
+  }
+  const bool side = fabsf(w_min) > fabsf(w_max);
+  float scale = mlx_max(__fdiv_rn(__fsub_rn(w_max, w_min), n_bins), eps);
+  scale = side ? scale : -scale;
+  const float edge = side ? w_min : w_max;
+  const float q0 = rintf(__fdiv_rn(edge, scale));
+  float bias = 0.0f;
+  if (q0 != 0.0f) {
+    scale = __fdiv_rn(edge, q0);
+    bias = edge;
+  }
+  // q = rint(fl((v - bias) / scale)) without a division per element.  With
+  // rs = fl(1 / scale) and y = fl(d * rs), |y - fl(d / scale)| is at most
+  // 1.5 * 2^-23 * |d / scale|: below 2^-14 * 0.75 while |y| < 512, and the
+  // codes of a group keep |y| near [0, 2^bits - 1].  So rint(y) is the
+  // answer unless y lies within 2^-12 of a half-integer (where the rounding
+  // of the quotient itself decides), is not finite, or is that large.  Of
+  // those, an exact quotient (d - y * scale == 0 by one fma, d normal) is y
+  // itself; the rest, about 0.05-0.2 % of elements, take the IEEE division.
+  const float rs = __frcp_rn(scale);
+  uint32_t packed[BITS / 4] = {};
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float d = __fsub_rn(v[j], bias);
+    const float y = __fmul_rn(d, rs);
+    float q = rintf(y);
+    const float margin = 0.5f - fabsf(__fsub_rn(y, q));
+    if (!(margin > 0x1p-12f) || !(fabsf(y) < 512.0f)) {
+      const bool exact = fabsf(y) < 512.0f && fabsf(d) > 0x1p-100f &&
+                         __fmaf_rn(-y, scale, d) == 0.0f;
+      if (!exact) q = rintf(__fdiv_rn(d, scale));
+    }
+    q = mlx_min(mlx_max(q, 0.0f), n_bins);
+    const uint32_t code = (q == q) ? static_cast<uint32_t>(q) : 0u;
+    if constexpr (BITS == 4) {
+      packed[0] |= code << (4 * j);
+    } else {
+      packed[j >> 2] |= code << (8 * (j & 3));
+    }
+  }
+  if (live) {
+    if constexpr (BITS == 4) {
+      codes[vi] = packed[0];
+    } else {
+      reinterpret_cast<uint2*>(codes)[vi] = make_uint2(packed[0], packed[1]);
+    }
+    if ((lane & (LANES - 1)) == 0) {
+      const int64_t gi = vi / LANES;
+      scales[gi] = f32_to_bf16_bits(scale);
+      biases[gi] = f32_to_bf16_bits(bias);
+    }
+  }
+}
+
+// Each warp takes two blocks of 32 consecutive vectors per iteration and
+// loads both before working on either, so two 16-byte loads per thread are
+// in flight.
 template <int BITS, int LANES>
 __global__ void __launch_bounds__(256) quantize_kernel(const uint4* __restrict__ w,
                                                        int64_t n_vec, uint32_t* __restrict__ codes,
                                                        uint16_t* __restrict__ scales,
                                                        uint16_t* __restrict__ biases) {
-  constexpr float n_bins = static_cast<float>((1 << BITS) - 1);
-  constexpr float eps = 1e-7f;
   const int lane = threadIdx.x & 31;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  // Iterate whole warps so shuffles always see 32 lanes.
-  for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x * 2;
+  for (int64_t base = (static_cast<int64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31)) * 2;
        base < n_vec; base += stride) {
-    const int64_t vi = base + lane;
-    const bool live = vi < n_vec;
-    uint4 raw = make_uint4(0, 0, 0, 0);
-    if (live) raw = __ldg(w + vi);
-    const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
-    float v[8];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      v[2 * j] = bf16_bits_to_f32(words[j] & 0xFFFFu);
-      v[2 * j + 1] = bf16_bits_to_f32(words[j] >> 16);
-    }
-    float w_max = -INFINITY, w_min = INFINITY;
-    if (live) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        w_max = mlx_max(w_max, v[j]);
-        w_min = mlx_min(w_min, v[j]);
-      }
-    }
-#pragma unroll
-    for (int off = 1; off < LANES; off <<= 1) {
-      w_max = mlx_max(w_max, __shfl_xor_sync(0xffffffffu, w_max, off));
-      w_min = mlx_min(w_min, __shfl_xor_sync(0xffffffffu, w_min, off));
-    }
-    const bool side = fabsf(w_min) > fabsf(w_max);
-    float scale = mlx_max(__fdiv_rn(__fsub_rn(w_max, w_min), n_bins), eps);
-    scale = side ? scale : -scale;
-    const float edge = side ? w_min : w_max;
-    const float q0 = rintf(__fdiv_rn(edge, scale));
-    float bias = 0.0f;
-    if (q0 != 0.0f) {
-      scale = __fdiv_rn(edge, q0);
-      bias = edge;
-    }
-    uint32_t packed[BITS / 4] = {};
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float q = rintf(__fdiv_rn(__fsub_rn(v[j], bias), scale));
-      q = mlx_min(mlx_max(q, 0.0f), n_bins);
-      const uint32_t code = (q == q) ? static_cast<uint32_t>(q) : 0u;
-      if constexpr (BITS == 4) {
-        packed[0] |= code << (4 * j);
-      } else {
-        packed[j >> 2] |= code << (8 * (j & 3));
-      }
-    }
-    if (live) {
-      if constexpr (BITS == 4) {
-        codes[vi] = packed[0];
-      } else {
-        reinterpret_cast<uint2*>(codes)[vi] = make_uint2(packed[0], packed[1]);
-      }
-      if ((lane & (LANES - 1)) == 0) {
-        const int64_t gi = vi / LANES;
-        scales[gi] = f32_to_bf16_bits(scale);
-        biases[gi] = f32_to_bf16_bits(bias);
-      }
-    }
+    const int64_t v0 = base + lane, v1 = base + 32 + lane;
+    const bool l0 = v0 < n_vec, l1 = v1 < n_vec;
+    uint4 r0 = make_uint4(0, 0, 0, 0), r1 = make_uint4(0, 0, 0, 0);
+    if (l0) r0 = __ldg(w + v0);
+    if (l1) r1 = __ldg(w + v1);
+    quantize_vector<BITS, LANES>(r0, l0, v0, lane, codes, scales, biases);
+    quantize_vector<BITS, LANES>(r1, l1, v1, lane, codes, scales, biases);
   }
 }
 
@@ -108,30 +139,43 @@ __global__ void __launch_bounds__(256) dequantize_kernel(const uint4* __restrict
                                                          const uint16_t* __restrict__ scales,
                                                          const uint16_t* __restrict__ biases,
                                                          uint4* __restrict__ out) {
-  constexpr int kElems = 4 * 32 / BITS;  // elements per thread
+  constexpr int kElems = 4 * 32 / BITS;  // elements per 16-byte load
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t qi = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; qi < n_quads;
-       qi += stride) {
-    const uint4 c = __ldg(codes + qi);
-    const int64_t first = qi * kElems;       // flat element index (group never straddled)
-    const int64_t gi = first >> group_shift;
-    const uint32_t s2 = bf16_dup(__ldg(scales + gi));
-    const uint32_t b2 = bf16_dup(__ldg(biases + gi));
-    const uint32_t words[4] = {c.x, c.y, c.z, c.w};
-    if constexpr (BITS == 4) {
+  // Two 16-byte loads (and their groups' scale and bias) in flight per
+  // thread: quads q and q + stride, then the next pair.
+  for (int64_t q2 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; q2 < n_quads;
+       q2 += 2 * stride) {
+    const bool second = q2 + stride < n_quads;
+    uint4 cc[2];
+    uint32_t s2[2], b2[2];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t o[4];
-        dequant_u4x8(words[j], s2, b2, o);
-        out[qi * 4 + j] = make_uint4(o[0], o[1], o[2], o[3]);
-      }
-    } else {
+    for (int h = 0; h < 2; ++h) {
+      const int64_t qi = h ? (second ? q2 + stride : q2) : q2;
+      cc[h] = __ldg(codes + qi);
+      const int64_t gi = (qi * kElems) >> group_shift;  // a group never straddles a quad
+      s2[h] = bf16_dup(__ldg(scales + gi));
+      b2[h] = bf16_dup(__ldg(biases + gi));
+    }
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        uint32_t o0[2], o1[2];
-        dequant_u8x4(words[2 * j], s2, b2, o0);
-        dequant_u8x4(words[2 * j + 1], s2, b2, o1);
-        out[qi * 2 + j] = make_uint4(o0[0], o0[1], o1[0], o1[1]);
+    for (int h = 0; h < 2; ++h) {
+      if (h == 1 && !second) break;
+      const int64_t qi = q2 + h * stride;
+      const uint32_t words[4] = {cc[h].x, cc[h].y, cc[h].z, cc[h].w};
+      if constexpr (BITS == 4) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t o[4];
+          dequant_u4x8(words[j], s2[h], b2[h], o);
+          out[qi * 4 + j] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          uint32_t o0[2], o1[2];
+          dequant_u8x4(words[2 * j], s2[h], b2[h], o0);
+          dequant_u8x4(words[2 * j + 1], s2[h], b2[h], o1);
+          out[qi * 2 + j] = make_uint4(o0[0], o0[1], o1[0], o1[1]);
+        }
       }
     }
   }
@@ -172,7 +216,7 @@ extern "C" int tq_quantize(const void* w, int64_t rows, int64_t cols, int group_
     return fail(TQ_ERR_MISALIGNED, "scales and biases must be 2-byte aligned");
   const int64_t n_vec = rows * cols / 8;
   const int block = 256;
-  const int grid = grid_for(n_vec, block);
+  const int grid = grid_for((n_vec + 1) / 2, block);  // two vectors per thread
   cudaStream_t s = as_stream(stream);
   const uint4* wv = static_cast<const uint4*>(w);
   uint32_t* c = static_cast<uint32_t*>(codes);
@@ -204,7 +248,7 @@ extern "C" int tq_dequantize(const void* codes, const void* scales, const void* 
   const int64_t n_words = rows * cols * bits / 32;
   const int64_t n_quads = n_words / 4;  // cols % 32 == 0 so n_words % 4 == 0
   const int block = 256;
-  const int grid = grid_for(n_quads, block);
+  const int grid = grid_for((n_quads + 1) / 2, block);  // two loads per thread
   const int shift = group_size == 32 ? 5 : (group_size == 64 ? 6 : 7);
   cudaStream_t s = as_stream(stream);
   if (bits == 4)
