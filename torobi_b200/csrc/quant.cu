@@ -3,8 +3,8 @@
 // Both are HBM-bound streams: quantize reads 2 bytes per element and writes
 // bits/8 + 4/group_size; dequantize the reverse.  Each thread owns whole
 // 16-byte vectors so every global access is a 128-bit transaction, and a
-// group's min/max is reduced across the group_size/16 lanes that hold it with
-// warp shuffles (groups never straddle a warp: 32 lanes x 16 elements covers
+// group's min/max is reduced across the group_size/32 lanes that hold it with
+// warp shuffles (groups never straddle a warp: 32 lanes x 32 elements covers
 // a whole number of groups for group_size in {32, 64, 128}).
 #include <cuda_bf16.h>
 
@@ -26,30 +26,39 @@ __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
   return static_cast<uint16_t>((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
 }
 
-// Quantizes 16 consecutive elements (two 16-byte vectors, r0 then r1) held by
-// lane `lane` of a warp whose 32 lanes hold 32 consecutive such pairs (pi is
-// this pair's index).  LANES = lanes per group = group_size / 16; a group's
-// min/max is reduced across its lanes with shuffles, so every lane of the
-// warp must call this.  Sixteen elements a thread halve the share of the
-// group's three divisions, which every lane of the group computes.
+// Quantizes 32 consecutive elements (four 16-byte vectors r[0..3]) held by
+// lane `lane` of a warp whose 32 lanes hold 32 consecutive such runs (pi is
+// this run's index).  LANES = lanes per group = group_size / 32 (1, 2 or 4);
+// a group's min/max is reduced across its lanes with shuffles, so every lane
+// of the warp must call this.  Thirty-two elements a thread spread the
+// group's three divisions, which every lane of the group computes, over four
+// times the elements of one vector a thread.
 template <int BITS, int LANES>
-__device__ __forceinline__ void quantize_pair(uint4 r0, uint4 r1, bool live, int64_t pi,
-                                              int lane, uint32_t* __restrict__ codes,
-                                              uint16_t* __restrict__ scales,
-                                              uint16_t* __restrict__ biases) {
+__device__ __forceinline__ void quantize_run(const uint4 (&r)[4], bool live, int64_t pi,
+                                             int lane, uint32_t* __restrict__ codes,
+                                             uint16_t* __restrict__ scales,
+                                             uint16_t* __restrict__ biases) {
+  constexpr int kE = 32;
   constexpr float n_bins = static_cast<float>((1 << BITS) - 1);
   constexpr float eps = 1e-7f;
-  const uint32_t words[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
-  float v[16];
+  uint32_t words[16];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
+  for (int k = 0; k < 4; ++k) {
+    words[4 * k] = r[k].x;
+    words[4 * k + 1] = r[k].y;
+    words[4 * k + 2] = r[k].z;
+    words[4 * k + 3] = r[k].w;
+  }
+  float v[kE];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
     v[2 * j] = bf16_bits_to_f32(words[j] & 0xFFFFu);
     v[2 * j + 1] = bf16_bits_to_f32(words[j] >> 16);
   }
   float w_max = -INFINITY, w_min = INFINITY;
   if (live) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
+    for (int j = 0; j < kE; ++j) {
       w_max = mlx_max(w_max, v[j]);
       w_min = mlx_min(w_min, v[j]);
     }
@@ -78,9 +87,9 @@ __device__ __forceinline__ void quantize_pair(uint4 r0, uint4 r1, bool live, int
   // those, an exact quotient (d - y * scale == 0 by one fma, d normal) is y
   // itself; the rest, about 0.05-0.2 % of elements, take the IEEE division.
   const float rs = __frcp_rn(scale);
-  uint32_t packed[BITS / 2] = {};
+  uint32_t packed[BITS] = {};  // 32 codes: 4 words at 4 bits, 8 at 8
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
+  for (int j = 0; j < kE; ++j) {
     const float d = __fsub_rn(v[j], bias);
     const float y = __fmul_rn(d, rs);
     float q = rintf(y);
@@ -99,11 +108,9 @@ __device__ __forceinline__ void quantize_pair(uint4 r0, uint4 r1, bool live, int
     }
   }
   if (live) {
-    if constexpr (BITS == 4) {
-      reinterpret_cast<uint2*>(codes)[pi] = make_uint2(packed[0], packed[1]);
-    } else {
-      reinterpret_cast<uint4*>(codes)[pi] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-    }
+    uint4* out = reinterpret_cast<uint4*>(codes) + pi * (BITS / 4);
+    out[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    if constexpr (BITS == 8) out[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
     if ((lane & (LANES - 1)) == 0) {
       const int64_t gi = pi / LANES;
       scales[gi] = f32_to_bf16_bits(scale);
@@ -112,25 +119,23 @@ __device__ __forceinline__ void quantize_pair(uint4 r0, uint4 r1, bool live, int
   }
 }
 
-// Each warp takes 32 consecutive pairs of vectors per iteration; both loads
-// of a thread's pair are in flight before it works on either.
+// Each warp takes 32 consecutive runs of 32 elements per iteration; the four
+// loads of a thread's run are in flight before it works on any.
 template <int BITS, int LANES>
 __global__ void __launch_bounds__(256) quantize_kernel(const uint4* __restrict__ w,
-                                                       int64_t n_pairs, uint32_t* __restrict__ codes,
+                                                       int64_t n_runs, uint32_t* __restrict__ codes,
                                                        uint16_t* __restrict__ scales,
                                                        uint16_t* __restrict__ biases) {
   const int lane = threadIdx.x & 31;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31);
-       base < n_pairs; base += stride) {
+       base < n_runs; base += stride) {
     const int64_t pi = base + lane;
-    const bool live = pi < n_pairs;
-    uint4 r0 = make_uint4(0, 0, 0, 0), r1 = make_uint4(0, 0, 0, 0);
-    if (live) {
-      r0 = __ldg(w + 2 * pi);
-      r1 = __ldg(w + 2 * pi + 1);
-    }
-    quantize_pair<BITS, LANES>(r0, r1, live, pi, lane, codes, scales, biases);
+    const bool live = pi < n_runs;
+    uint4 r[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) r[k] = live ? __ldg(w + 4 * pi + k) : make_uint4(0, 0, 0, 0);
+    quantize_run<BITS, LANES>(r, live, pi, lane, codes, scales, biases);
   }
 }
 
@@ -216,23 +221,23 @@ extern "C" int tq_quantize(const void* w, int64_t rows, int64_t cols, int group_
     return fail(TQ_ERR_MISALIGNED, "w and codes must be 16-byte aligned");
   if (!aligned(scales, 2) || !aligned(biases, 2))
     return fail(TQ_ERR_MISALIGNED, "scales and biases must be 2-byte aligned");
-  const int64_t n_pairs = rows * cols / 16;  // cols % 32 == 0
+  const int64_t n_runs = rows * cols / 32;  // cols % 32 == 0
   const int block = 256;
-  const int grid = grid_for(n_pairs, block);
+  const int grid = grid_for(n_runs, block);
   cudaStream_t s = as_stream(stream);
   const uint4* wv = static_cast<const uint4*>(w);
   uint32_t* c = static_cast<uint32_t*>(codes);
   uint16_t* sc = static_cast<uint16_t*>(scales);
   uint16_t* bi = static_cast<uint16_t*>(biases);
-  const int lanes = group_size / 16;
+  const int lanes = group_size / 32;
   if (bits == 4) {
-    if (lanes == 2) quantize_kernel<4, 2><<<grid, block, 0, s>>>(wv, n_pairs, c, sc, bi);
-    else if (lanes == 4) quantize_kernel<4, 4><<<grid, block, 0, s>>>(wv, n_pairs, c, sc, bi);
-    else quantize_kernel<4, 8><<<grid, block, 0, s>>>(wv, n_pairs, c, sc, bi);
+    if (lanes == 1) quantize_kernel<4, 1><<<grid, block, 0, s>>>(wv, n_runs, c, sc, bi);
+    else if (lanes == 2) quantize_kernel<4, 2><<<grid, block, 0, s>>>(wv, n_runs, c, sc, bi);
+    else quantize_kernel<4, 4><<<grid, block, 0, s>>>(wv, n_runs, c, sc, bi);
   } else {
-    if (lanes == 2) quantize_kernel<8, 2><<<grid, block, 0, s>>>(wv, n_pairs, c, sc, bi);
-    else if (lanes == 4) quantize_kernel<8, 4><<<grid, block, 0, s>>>(wv, n_pairs, c, sc, bi);
-    else quantize_kernel<8, 8><<<grid, block, 0, s>>>(wv, n_pairs, c, sc, bi);
+    if (lanes == 1) quantize_kernel<8, 1><<<grid, block, 0, s>>>(wv, n_runs, c, sc, bi);
+    else if (lanes == 2) quantize_kernel<8, 2><<<grid, block, 0, s>>>(wv, n_runs, c, sc, bi);
+    else quantize_kernel<8, 4><<<grid, block, 0, s>>>(wv, n_runs, c, sc, bi);
   }
   return check_cuda(cudaGetLastError(), "quantize launch");
 }
