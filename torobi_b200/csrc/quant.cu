@@ -139,50 +139,47 @@ __global__ void __launch_bounds__(256) quantize_kernel(const uint4* __restrict__
   }
 }
 
-// One thread = 4 code words.  4-bit: 32 elements (64 B out); 8-bit: 16 (32 B).
+// One code word a lane per step (8 elements at 4 bits, 4 at 8), so a warp
+// reads 128 contiguous bytes and writes 512 (256) contiguous bytes per
+// instruction; each thread takes kWords words, 32 apart, all loaded (with
+// their groups' scale and bias) before any is dequantized.
+constexpr int kWords = 8;
+
 template <int BITS>
-__global__ void __launch_bounds__(256) dequantize_kernel(const uint4* __restrict__ codes,
-                                                         int64_t n_quads, int group_shift,
+__global__ void __launch_bounds__(256) dequantize_kernel(const uint32_t* __restrict__ codes,
+                                                         int64_t n_words, int group_shift,
                                                          const uint16_t* __restrict__ scales,
                                                          const uint16_t* __restrict__ biases,
-                                                         uint4* __restrict__ out) {
-  constexpr int kElems = 4 * 32 / BITS;  // elements per 16-byte load
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  // Two 16-byte loads (and their groups' scale and bias) in flight per
-  // thread: quads q and q + stride, then the next pair.
-  for (int64_t q2 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; q2 < n_quads;
-       q2 += 2 * stride) {
-    const bool second = q2 + stride < n_quads;
-    uint4 cc[2];
-    uint32_t s2[2], b2[2];
+                                                         uint16_t* __restrict__ out) {
+  constexpr int kElems = 32 / BITS;  // elements per word
+  const int lane = threadIdx.x & 31;
+  const int64_t span = 32 * kWords;  // words a warp covers per iteration
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t base = (static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) *
+                      span;
+       base < n_words; base += warps * span) {
+    uint32_t c[kWords], s2[kWords], b2[kWords];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int64_t qi = h ? (second ? q2 + stride : q2) : q2;
-      cc[h] = __ldg(codes + qi);
-      const int64_t gi = (qi * kElems) >> group_shift;  // a group never straddles a quad
-      s2[h] = bf16_dup(__ldg(scales + gi));
-      b2[h] = bf16_dup(__ldg(biases + gi));
+    for (int k = 0; k < kWords; ++k) {
+      const int64_t wi = base + 32 * k + lane;
+      const bool live = wi < n_words;
+      c[k] = live ? __ldg(codes + wi) : 0u;
+      const int64_t gi = live ? (wi * kElems) >> group_shift : 0;  // a group never straddles a word
+      s2[k] = bf16_dup(__ldg(scales + gi));
+      b2[k] = bf16_dup(__ldg(biases + gi));
     }
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      if (h == 1 && !second) break;
-      const int64_t qi = q2 + h * stride;
-      const uint32_t words[4] = {cc[h].x, cc[h].y, cc[h].z, cc[h].w};
+    for (int k = 0; k < kWords; ++k) {
+      const int64_t wi = base + 32 * k + lane;
+      if (wi >= n_words) break;
       if constexpr (BITS == 4) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint32_t o[4];
-          dequant_u4x8(words[j], s2[h], b2[h], o);
-          out[qi * 4 + j] = make_uint4(o[0], o[1], o[2], o[3]);
-        }
+        uint32_t o[4];
+        dequant_u4x8(c[k], s2[k], b2[k], o);
+        reinterpret_cast<uint4*>(out)[wi] = make_uint4(o[0], o[1], o[2], o[3]);
       } else {
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          uint32_t o0[2], o1[2];
-          dequant_u8x4(words[2 * j], s2[h], b2[h], o0);
-          dequant_u8x4(words[2 * j + 1], s2[h], b2[h], o1);
-          out[qi * 2 + j] = make_uint4(o0[0], o0[1], o1[0], o1[1]);
-        }
+        uint32_t o[2];
+        dequant_u8x4(c[k], s2[k], b2[k], o);
+        reinterpret_cast<uint2*>(out)[wi] = make_uint2(o[0], o[1]);
       }
     }
   }
@@ -253,18 +250,17 @@ extern "C" int tq_dequantize(const void* codes, const void* scales, const void* 
   if (!aligned(w, 16) || !aligned(codes, 16))
     return fail(TQ_ERR_MISALIGNED, "w and codes must be 16-byte aligned");
   const int64_t n_words = rows * cols * bits / 32;
-  const int64_t n_quads = n_words / 4;  // cols % 32 == 0 so n_words % 4 == 0
   const int block = 256;
-  const int grid = grid_for((n_quads + 1) / 2, block);  // two loads per thread
+  const int grid = grid_for((n_words + kWords - 1) / kWords, block);
   const int shift = group_size == 32 ? 5 : (group_size == 64 ? 6 : 7);
   cudaStream_t s = as_stream(stream);
+  const uint32_t* cw = static_cast<const uint32_t*>(codes);
+  const uint16_t* sp = static_cast<const uint16_t*>(scales);
+  const uint16_t* bp = static_cast<const uint16_t*>(biases);
+  uint16_t* op = static_cast<uint16_t*>(w);
   if (bits == 4)
-    dequantize_kernel<4><<<grid, block, 0, s>>>(
-        static_cast<const uint4*>(codes), n_quads, shift, static_cast<const uint16_t*>(scales),
-        static_cast<const uint16_t*>(biases), static_cast<uint4*>(w));
+    dequantize_kernel<4><<<grid, block, 0, s>>>(cw, n_words, shift, sp, bp, op);
   else
-    dequantize_kernel<8><<<grid, block, 0, s>>>(
-        static_cast<const uint4*>(codes), n_quads, shift, static_cast<const uint16_t*>(scales),
-        static_cast<const uint16_t*>(biases), static_cast<uint4*>(w));
+    dequantize_kernel<8><<<grid, block, 0, s>>>(cw, n_words, shift, sp, bp, op);
   return check_cuda(cudaGetLastError(), "dequantize launch");
 }
