@@ -721,7 +721,7 @@ Plan make_plan(const Args& a, bool allow_split) {
     const char* e = getenv("TQ_QMM_PAIR");
     return e && e[0] == '0';
   }();
-  if (!pair_off && pl.stma && pl.splits == 1 && n_out > kBM) {
+  if (!pair_off && pl.stma && pl.splits == 1 && n_out > kBM && aligned(a.y, 16)) {
     const int64_t pair_tiles_n = (n_out + 2 * kBM - 1) / (2 * kBM);
     const int pairs = sm_count() / 2;
     const int forced = forced_bn();
@@ -953,6 +953,17 @@ int launch_pair(const Args& a, const Plan& pl, cudaStream_t stream, int* status)
   int rc = make_maps<BITS, TRANS>(a, BN / 2, C::SC_ROWS, true, mp);
   if (rc) return rc;
   const Params p = make_params(a, pl, kPairRows, BN, status);
+  // y as the epilogue's TMA store target: boxes of 32 features x 32 tokens.
+  CUtensorMap tm_y;
+  {
+    const int64_t n_out = TRANS ? a.w_rows : a.w_cols;
+    const uint64_t dims[2] = {static_cast<uint64_t>(n_out), static_cast<uint64_t>(a.m)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(n_out) * 2};
+    const uint32_t box[2] = {32, 32};
+    rc = encode_tmap(&tm_y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.y, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  }
   auto kernel = qmm_pair_kernel<BITS, TRANS, BN, G>;
   rc = set_max_smem_once(reinterpret_cast<const void*>(kernel), C::SMEM,
                          "cudaFuncSetAttribute(qmm pair smem)");
@@ -971,8 +982,9 @@ int launch_pair(const Args& a, const Plan& pl, cudaStream_t stream, int* status)
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return check_cuda(cudaLaunchKernelEx(&cfg, kernel, mp.x, mp.c, mp.lup, mp.ldn, mp.sc, mp.bi, p),
-                    "qmm pair launch");
+  return check_cuda(
+      cudaLaunchKernelEx(&cfg, kernel, mp.x, mp.c, mp.lup, mp.ldn, mp.sc, mp.bi, tm_y, p),
+      "qmm pair launch");
 }
 
 template <int BITS, bool TRANS>

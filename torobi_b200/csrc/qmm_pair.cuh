@@ -42,7 +42,11 @@ struct PairCfg {
   static constexpr int LDN_BYTES = XH_ROWS * 16 * 2;        // [BN/2 x 16] bf16
   static constexpr int LORA_BYTES = ((LUP_BYTES + LDN_BYTES + 1023) / 1024) * 1024;
   static constexpr int BAR_BYTES = 512;
-  static constexpr int FIXED = 1024 + LORA_BYTES + BAR_BYTES;
+  // Epilogue staging: per epilogue warp two [32 tokens x 32 features] bf16
+  // buffers, written from TMEM and stored to y by TMA.
+  static constexpr int EPI_CHUNK = 32 * 32 * 2;
+  static constexpr int EPI_BYTES = 4 * 2 * EPI_CHUNK;
+  static constexpr int FIXED = 1024 + LORA_BYTES + EPI_BYTES + BAR_BYTES;
   // G dequantizing groups on alternate k-steps, one weight-tile buffer more.
   static constexpr int DQ_GROUPS = G;
   static constexpr int stages_with(int a) { return (kSmemLimit - FIXED - a * A_BYTES) / STAGE_BYTES; }
@@ -75,7 +79,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __grid_constant__ CUtensorMap tm_lup,
                     const __grid_constant__ CUtensorMap tm_ldn,
                     const __grid_constant__ CUtensorMap tm_sc,
-                    const __grid_constant__ CUtensorMap tm_bi, const Params p) {
+                    const __grid_constant__ CUtensorMap tm_bi,
+                    const __grid_constant__ CUtensorMap tm_y, const Params p) {
   using C = PairCfg<BITS, TRANS, BN, G>;
   constexpr int S = C::STAGES;
   constexpr int A = C::A_BUFS;
@@ -87,7 +92,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Same offsets in both CTAs (the pair UMMA reads the peer at the leader's).
   const uint32_t lup = base;
   const uint32_t ldn = base + C::LUP_BYTES;
-  const uint32_t abufs = base + C::LORA_BYTES;
+  const uint32_t epi = base + C::LORA_BYTES;                       // epilogue staging
+  const uint32_t abufs = epi + C::EPI_BYTES;
   const uint32_t stages = abufs + A * C::A_BYTES;
   auto a_s = [&](int a) { return abufs + a * C::A_BYTES; };
   auto x_s = [&](int s) { return stages + s * C::STAGE_BYTES; };
@@ -314,39 +320,57 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // Each 32-token chunk of this warp's 32 features goes through one of its
+    // two staging buffers ([token][feature] bf16) and out by a TMA store,
+    // which clips tokens past m and features past n_out.
     const int q = warp & 3;
     const int r = q * 32 + lane;
+    const uint32_t stage_w = epi + static_cast<uint32_t>(q) * 2 * C::EPI_CHUNK;
+    if (lane == 0) tma_prefetch_desc(&tm_y);
     bool ok = true;
+    int chunk = 0;
     for (int lt = 0; lt < my_tiles && ok; ++lt) {
       const int buf = lt & 1;
       ok = mbar_wait(acc_full(buf), (lt >> 1) & 1, p.status);
       tc_fence_after();
-      const int og = tile_out0(lt) + r;
+      const int og0 = tile_out0(lt) + q * 32;
+      const int og = og0 + lane;
       const int m0 = tile_m0(lt);
       float bias = 0.0f;
       if (p.bias_vec && og < p.n_out)
         bias = __uint_as_float(uint32_t(ldg_u16(p.bias_vec + og)) << 16);
       const uint32_t d = tmem + buf * C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16);
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      for (int c0 = 0; c0 < BN; c0 += 32, ++chunk) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(d + c0, v);
         tmem_ld_wait();
-        if (ok && og < p.n_out) {
-          const int mlim = p.m - (m0 + c0);
-          uint16_t* yp = p.y + static_cast<size_t>(m0 + c0) * p.n_out + og;
+        if (!ok) continue;
+        const uint32_t sb = stage_w + static_cast<uint32_t>(chunk & 1) * C::EPI_CHUNK;
+        // The store issued from this buffer two chunks ago has read it.
+        if (lane == 0) tma_store_wait_read1();
+        __syncwarp();
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            if (jj < mlim)
-              yp[static_cast<size_t>(jj) * p.n_out] =
-                  __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[jj]) + bias));
-          }
+        for (int jj = 0; jj < 32; ++jj)
+          sts16(sb + jj * 64 + lane * 2,
+                __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[jj]) + bias)));
+        fence_proxy_async_smem();
+        __syncwarp();
+        // One group per chunk (empty when the box lies wholly past y), so
+        // "all but the newest group have read" always covers this buffer's
+        // previous store.
+        if (lane == 0) {
+          if (og0 < p.n_out && m0 + c0 < p.m) tma_store_2d(&tm_y, sb, og0, m0 + c0);
+          tma_store_commit();
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(lead(acc_empty(buf)));
     }
+    // The staging buffers stay valid until every store has read them.
+    if (lane == 0) tma_store_wait_all();
+    __syncwarp();
   }
   // Both CTAs done with every barrier, copy and accumulator before TMEM is
   // freed and either CTA exits.
