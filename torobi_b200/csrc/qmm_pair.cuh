@@ -50,7 +50,13 @@ struct PairCfg {
   // G dequantizing groups on alternate k-steps, one weight-tile buffer more.
   static constexpr int DQ_GROUPS = G;
   static constexpr int stages_with(int a) { return (kSmemLimit - FIXED - a * A_BYTES) / STAGE_BYTES; }
-  static constexpr int A_BUFS = stages_with(G + 1) >= 4 ? G + 1 : (stages_with(3) >= 4 ? 3 : 2);
+  // A buffer per group and one for the MMA, unless that leaves fewer than
+  // six TMA stages and one buffer fewer does not.
+  static constexpr int A_BUFS =
+      stages_with(G + 1) >= 6 ? G + 1
+      : stages_with(G) >= 6   ? G
+      : stages_with(G + 1) >= 4 ? G + 1
+                                : (stages_with(3) >= 4 ? 3 : 2);
   static constexpr int STAGES_RAW = (kSmemLimit - FIXED - A_BUFS * A_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr int SMEM = FIXED + A_BUFS * A_BYTES + STAGES * STAGE_BYTES;
