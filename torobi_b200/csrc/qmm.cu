@@ -67,7 +67,11 @@ struct Cfg {
   static constexpr int LDN_BYTES = BN * 16 * 2;             // [BN x 16] bf16
   static constexpr int LORA_BYTES = ((LUP_BYTES + LDN_BYTES + 1023) / 1024) * 1024;
   static constexpr int BAR_BYTES = 512;
-  static constexpr int FIXED = 1024 + LORA_BYTES + BAR_BYTES;
+  // Epilogue staging: per epilogue warp two [32 tokens x 32 features] bf16
+  // buffers, written from TMEM and stored to y by TMA.
+  static constexpr int EPI_CHUNK = 32 * 32 * 2;
+  static constexpr int EPI_BYTES = 4 * 2 * EPI_CHUNK;
+  static constexpr int FIXED = 1024 + LORA_BYTES + EPI_BYTES + BAR_BYTES;
   // Dequantizing groups on alternate k-steps: with scale tiles, two for the
   // large token tiles (the MMA is long) and four for the small ones (the
   // MMA is short and the dequantization's latency is the whole step); one
@@ -104,6 +108,7 @@ struct Params {
   int splits;                // k-splits per tile (split-K); 1 = none
   int k_steps_per_split;     // k-steps of every split but maybe the last
   float* ws;                 // splits > 1: f32 partials [splits, m, n_out]
+  int tma_y;                 // the bf16 output goes out through TMA stores (tm_y)
   int* status;
 };
 
@@ -294,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     qmm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_c,
                const __grid_constant__ CUtensorMap tm_lup, const __grid_constant__ CUtensorMap tm_ldn,
                const __grid_constant__ CUtensorMap tm_sc, const __grid_constant__ CUtensorMap tm_bi,
-               const Params p) {
+               const __grid_constant__ CUtensorMap tm_y, const Params p) {
   using C = Cfg<BITS, TRANS, BN, STMA>;
   constexpr int S = C::STAGES;
   constexpr int A = C::A_BUFS;
@@ -305,7 +310,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const uint32_t lup = base;                                  // LoRA up tile
   const uint32_t ldn = base + C::LUP_BYTES;                   // LoRA down tile
-  const uint32_t abufs = base + C::LORA_BYTES;                // dequantized-weight ring
+  const uint32_t epi = base + C::LORA_BYTES;                  // epilogue staging
+  const uint32_t abufs = epi + C::EPI_BYTES;                  // dequantized-weight ring
   const uint32_t stages = abufs + A * C::A_BYTES;             // TMA stage ring
   auto a_s = [&](int a) { return abufs + a * C::A_BYTES; };
   auto x_s = [&](int s) { return stages + s * C::STAGE_BYTES; };
@@ -581,6 +587,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;              // TMEM lane quadrant this warp may read
     const int r = q * 32 + lane;         // output feature within the tile
+    // With tma_y, each 32-token chunk of this warp's 32 features goes through
+    // one of its two staging buffers ([token][feature] bf16) and out by a TMA
+    // store, clipped at y's edges; one bulk group per chunk (empty when the
+    // box lies wholly past y) keeps "all but the newest group have read"
+    // covering the buffer about to be reused.
+    const uint32_t stage_w = epi + static_cast<uint32_t>(q) * 2 * C::EPI_CHUNK;
+    if (p.tma_y && lane == 0) tma_prefetch_desc(&tm_y);
+    int chunk = 0;
     bool ok = true;
     for (int lt = 0; lt < my_tiles && ok; ++lt) {
       const int buf = lt & 1;
@@ -597,7 +611,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t v[32];
         tmem_ld_32x32b_x32(d + c0, v);
         tmem_ld_wait();
-        if (ok && og < p.n_out) {
+        if (ok && p.tma_y) {
+          const uint32_t sb = stage_w + static_cast<uint32_t>(chunk & 1) * C::EPI_CHUNK;
+          ++chunk;
+          if (lane == 0) tma_store_wait_read1();
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            sts16(sb + j * 64 + lane * 2,
+                  __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[j]) + bias)));
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const int og0 = out0 + q * 32;
+            if (og0 < p.n_out && m0 + c0 < p.m) tma_store_2d(&tm_y, sb, og0, m0 + c0);
+            tma_store_commit();
+          }
+        } else if (ok && og < p.n_out) {
           const int mlim = p.m - (m0 + c0);
           if (p.splits > 1) {
             // f32 partial of this split; the reduce kernel adds bias and rounds.
@@ -620,6 +650,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty(buf));
     }
+    // The staging buffers stay valid until every store has read them.
+    if (p.tma_y && lane == 0) tma_store_wait_all();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -876,6 +909,7 @@ Params make_params(const Args& a, const Plan& pl, int tile_rows, int bn, int* st
   p.splits = pl.splits;
   p.k_steps_per_split = pl.k_steps_per_split;
   p.ws = static_cast<float*>(a.ws);
+  p.tma_y = 0;
   p.status = status;
   return p;
 }
@@ -887,14 +921,27 @@ int launch(const Args& a, const Plan& pl, cudaStream_t stream, int* status) {
   Maps mp;
   int rc = make_maps<BITS, TRANS>(a, BN, C::SC_ROWS, STMA, mp);
   if (rc) return rc;
-  const Params p = make_params(a, pl, kBM, BN, status);
+  Params p = make_params(a, pl, kBM, BN, status);
+  // Without a split the bf16 output goes out by TMA stores when y allows it
+  // (16-byte aligned; the row pitch is n_out * 2 bytes, a multiple of 16).
+  CUtensorMap tm_y = mp.x;
+  p.tma_y = 0;
+  if (pl.splits == 1 && aligned(a.y, 16)) {
+    const uint64_t dims[2] = {static_cast<uint64_t>(n_out), static_cast<uint64_t>(a.m)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(n_out) * 2};
+    const uint32_t box[2] = {32, 32};
+    rc = encode_tmap(&tm_y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.y, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    p.tma_y = 1;
+  }
   auto kernel = qmm_kernel<BITS, TRANS, BN, STMA>;
   rc = set_max_smem_once(reinterpret_cast<const void*>(kernel), C::SMEM,
                          "cudaFuncSetAttribute(qmm smem)");
   if (rc) return rc;
   const int units = p.tiles_total * p.splits;
   const int grid = units < sm_count() ? units : sm_count();
-  kernel<<<grid, kThreads, C::SMEM, stream>>>(mp.x, mp.c, mp.lup, mp.ldn, mp.sc, mp.bi, p);
+  kernel<<<grid, kThreads, C::SMEM, stream>>>(mp.x, mp.c, mp.lup, mp.ldn, mp.sc, mp.bi, tm_y, p);
   rc = check_cuda(cudaGetLastError(), "qmm launch");
   if (rc || pl.splits == 1) return rc;
   const int64_t nv = a.m * n_out / 8;
