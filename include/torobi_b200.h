@@ -58,6 +58,17 @@ const char* tq_last_error(void);
  */
 int tq_device_status(int* status_out, int clear);
 
+/*
+ * Test hook for the failure path: launches one bounded wait on an mbarrier
+ * that nothing arrives on.  After limit_ns (1 ms to 10 s) the wait runs out,
+ * sets the timeout bit (1) of the device status word and the kernel returns,
+ * as every kernel's bounded waits do when a producer is lost;
+ * tq_device_status then reports TQ_ERR_TIMEOUT.  No counterpart in the
+ * reference, whose engine surfaces MLX's errors instead
+ * (engine/src/mlxc/error.rs:1-80).
+ */
+int tq_wait_selftest(int64_t limit_ns, void* stream);
+
 /* ---------------------------------------------------------------- packing */
 
 /*

@@ -51,6 +51,7 @@ SIGNATURES = {
     "tq_version": ([], _i32),
     "tq_last_error": ([], ctypes.c_char_p),
     "tq_device_status": ([ctypes.POINTER(_i32), _i32], _i32),
+    "tq_wait_selftest": ([_i64, _vp], _i32),
     "tq_quantize": ([_vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _vp], _i32),
     "tq_dequantize": ([_vp, _vp, _vp, _i64, _i64, _i32, _i32, _vp, _vp], _i32),
     "tq_quantized_matmul": ([_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _i32, _vp, _vp],

@@ -88,13 +88,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity to complete.  On timeout
-// records kDevTimeout in *status and returns false.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* status) {
+// (limit_ns, 2 s unless given) records kDevTimeout in *status and returns
+// false.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* status,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 0; i < (1u << 30); ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63u) == 63u && globaltimer_ns() - t0 > kWaitLimitNs) break;
+    if ((i & 63u) == 63u && globaltimer_ns() - t0 > limit_ns) break;
   }
   if (status) atomicOr(status, kDevTimeout);
   return false;
