@@ -20,9 +20,10 @@ tensor peak.  ``cpu_baseline``: the CPU oracle on a bounded sample.
 
 Kernel workloads (one GPU): ``--workload qmm`` (one quantized_matmul shape),
 ``qmm-sweep`` (M x projection shapes, forward and dX), ``quant-sweep``
-(quantize/dequantize over every Qwen2.5-0.5B-shaped linear), ``merge`` (the
-export merge over a Llama-3-8B-shaped layer) and ``load`` (quantize-at-load
-of a published bf16 file).
+(quantize/dequantize over every Qwen2.5-0.5B-shaped linear), ``lora`` (the
+LoRA down-projections and adapter gradients of one Llama-3-8B-shaped layer
+and micro-batch), ``merge`` (the export merge over a Llama-3-8B-shaped layer)
+and ``load`` (quantize-at-load of a published bf16 file).
 """
 from __future__ import annotations
 
@@ -56,7 +57,8 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--workload", choices=("llama3-8b", "qwen2.5-0.5b", "qmm", "qmm-sweep",
-                                          "quant-sweep", "merge", "load"), default="llama3-8b")
+                                          "quant-sweep", "lora", "merge", "load"),
+                   default="llama3-8b")
     p.add_argument("--m", type=int, default=16384, help="qmm: tokens")
     p.add_argument("--n", type=int, default=4096, help="qmm: weight rows (out features)")
     p.add_argument("--k", type=int, default=4096, help="qmm: weight cols (in features)")
@@ -467,10 +469,18 @@ def run_kernels(args):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    # 1 GiB (> 126 MB of L2), long enough that the host has enqueued the timed
-    # launch before the flush ends, so the events time the device only.
+    # Write 1 GiB (> 126 MB of L2), then read another 1 GiB, so that L2 is
+    # left holding clean lines: a kernel timed after a write-only flush also
+    # pays for writing back the flush's dirty lines it evicts (up to 126 MB),
+    # which halves the apparent rate of an HBM-bound kernel of ~100 MB.  Long
+    # enough that the host has enqueued the timed launch before the flush
+    # ends, so the events time the device only.
     flush_buf = torch.empty(1024 * 1024 * 1024, dtype=torch.uint8, device=dev)
-    flush = lambda: flush_buf.zero_()  # noqa: E731
+    flush_src = torch.ones(256 * 1024 * 1024, dtype=torch.int32, device=dev)
+
+    def flush():
+        flush_buf.zero_()
+        flush_src.max()
     peaks, peak_kind = measured_peaks()
     burst = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
     hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
@@ -487,7 +497,7 @@ def run_kernels(args):
                           "config": {"workload": f"quantized_matmul {args.direction}",
                                      "m": args.m, "w_rows": args.n, "w_cols": args.k,
                                      "bits": args.bits, "group_size": 64,
-                                     "l2": "flushed before every launch"},
+                                     "l2": "flushed before every launch (clean)"},
                           "roofline": {"bound": "tensor", "achieved": tf, "peak": burst,
                                        "unit": "TFLOP/s", "frac": tf / burst,
                                        "peak_kind": f"{peak_kind} burst bf16"}}), flush=True)
@@ -515,7 +525,7 @@ def run_kernels(args):
                           "value": val, "unit": "TFLOP/s", "scaling": "weak", "dtype": "bf16",
                           **common,
                           "config": {"workload": "quantized_matmul shape sweep, 4-bit g64",
-                                     "l2": "flushed before every launch"},
+                                     "l2": "flushed before every launch (clean)"},
                           "roofline": {"bound": "tensor", "achieved": val, "peak": burst,
                                        "unit": "TFLOP/s", "frac": val / burst,
                                        "peak_kind": f"{peak_kind} burst bf16"},
@@ -554,11 +564,57 @@ def run_kernels(args):
                           "value": val, "unit": "GB/s", "scaling": "weak",
                           "dtype": "u4/u8 codes, bf16", **common,
                           "config": {"workload": "affine quantize/dequantize sweep",
-                                     "l2": "flushed before every launch"},
+                                     "l2": "flushed before every launch (clean)"},
                           "roofline": {"bound": "hbm", "achieved": val, "peak": hbm,
                                        "unit": "GB/s", "frac": val / hbm,
                                        "peak_kind": f"{peak_kind} copy"},
                           "sweep": rows}), flush=True)
+        return 0
+    if args.workload == "lora":
+        # The skinny LoRA launches of one Llama-3-8B-shaped layer for one
+        # micro-batch of 8192 tokens (rank 16): per linear [d_out, d_in], the
+        # forward down-projection x.A^T (reads x [8192, d_in]), the backward
+        # one dY.B (reads dY [8192, d_out]) and the two adapter gradients
+        # (dA reads x, dB reads dY).  HBM-bound on the big operand.
+        from torobi_b200 import ops
+        from torobi_b200.model import LLAMA3_8B
+
+        g = torch.Generator(device=dev)
+        g.manual_seed(0)
+        r, m = LLAMA3_8B.lora_rank, 8192
+        kinds = {"down": [0.0, 0.0], "grad": [0.0, 0.0]}
+        rows = []
+        for name, (o, i) in LLAMA3_8B.linear_shapes().items():
+            for side, c in (("x", i), ("dY", o)):
+                big = torch.randn(m, c, device=dev, generator=g).bfloat16()
+                a = (torch.randn(r, c, device=dev, generator=g) * 0.01).bfloat16()
+                _, p_t = ops.lora_down(big, a, 2.0)
+                ms_d = _time_kernel(lambda: ops.lora_down(big, a, 2.0), K, W, flush)
+                out = torch.empty(c, r, dtype=torch.float32, device=dev)
+                ms_g = _time_kernel(lambda: ops.lora_grad(big, p_t, 0, out=out), K, W, flush)
+                nb_d = m * c * 2 + 2 * m * r * 2
+                nb_g = m * c * 2 + r * m * 2 + c * r * 4
+                kinds["down"][0] += ms_d
+                kinds["down"][1] += nb_d
+                kinds["grad"][0] += ms_g
+                kinds["grad"][1] += nb_g
+                rows.append({"linear": name, "operand": side, "m": m, "k": c,
+                             "down_us": ms_d * 1e3, "down_gbs": nb_d / ms_d / 1e6,
+                             "grad_us": ms_g * 1e3, "grad_gbs": nb_g / ms_g / 1e6})
+                del big, a, p_t, out
+        total_ms = kinds["down"][0] + kinds["grad"][0]
+        val = (kinds["down"][1] + kinds["grad"][1]) / total_ms / 1e6
+        print(json.dumps({"metric": "LoRA skinny kernels GB/s (Llama-3-8B layer, 8192 tokens, r16)",
+                          "value": val, "unit": "GB/s", "scaling": "weak", "dtype": "bf16",
+                          **common,
+                          "config": {"workload": "lora_down + lora_grad over one layer",
+                                     "l2": "flushed before every launch (clean)"},
+                          "roofline": {"bound": "hbm", "achieved": val, "peak": hbm,
+                                       "unit": "GB/s", "frac": val / hbm,
+                                       "peak_kind": f"{peak_kind} copy"},
+                          "down_gbs": kinds["down"][1] / kinds["down"][0] / 1e6,
+                          "grad_gbs": kinds["grad"][1] / kinds["grad"][0] / 1e6,
+                          "launches": rows}), flush=True)
         return 0
     if args.workload == "merge":
         # The export merge over one Llama-3-8B-shaped layer's seven linears
@@ -589,7 +645,7 @@ def run_kernels(args):
                           "value": val, "unit": "GB/s", "scaling": "weak", "dtype": "u4 -> f32",
                           **common,
                           "config": {"workload": "dequantize + scale * B A, f32 out",
-                                     "l2": "flushed before every launch"},
+                                     "l2": "flushed before every launch (clean)"},
                           "roofline": {"bound": "hbm", "achieved": val, "peak": hbm,
                                        "unit": "GB/s", "frac": val / hbm,
                                        "peak_kind": f"{peak_kind} copy"},
@@ -644,7 +700,7 @@ def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference(args)
-    if args.workload in ("qmm", "qmm-sweep", "quant-sweep", "merge", "load"):
+    if args.workload in ("qmm", "qmm-sweep", "quant-sweep", "lora", "merge", "load"):
         return run_kernels(args)
     return run_ours(args)
 

@@ -139,3 +139,34 @@ def test_lora_grad_accumulates_micro_batches(cuda, oracle):
     ref = (p_t.float() @ x.float())
     assert torch.allclose(whole, ref, rtol=1e-4, atol=1e-3)
     assert torch.allclose(acc, ref, rtol=1e-4, atol=1e-3)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,k,r", [(8192, 4096, 16),   # q/k/v/o/gate/up: k split in two
+                                   (2048, 14336, 8),   # down_proj: four CTAs per row tile
+                                   (4096, 896, 16),    # 14 k steps over four CTAs
+                                   (300, 320, 16),     # 5 k steps over three, ragged rows
+                                   (128, 64, 8)])      # one k step: no split
+def test_lora_down_with_k_split_over_a_cluster(cuda, oracle, m, k, r):
+    """The down-projection RNE(scale * x.A^T) when k is split over a cluster
+    of CTAs (partials added in the leader's shared memory) against an f32
+    reference, and its transposed copy bit-equal to it.  Then the adapter
+    gradient x^T.P over the same x, one wave of CTAs each reducing a slice
+    of m (one slice per tile at k = 14336)."""
+    import torch
+    import torobi_b200 as tq
+
+    torch.manual_seed(11)
+    x = torch.randn(m, k, device=cuda).bfloat16()
+    a = (torch.randn(r, k, device=cuda) / 8).bfloat16()
+    out, out_t = tq.lora_down(x, a, 2.0)
+    want = (2.0 * (x.float() @ a.float().t())).cpu().numpy()
+    err = oracle.rel_err(out.float().cpu().numpy(), want)
+    assert err <= TOL, f"max rel err {err:.3e}"
+    assert torch.equal(out_t[:, :m], out.t())
+    again, _ = tq.lora_down(x, a, 2.0)
+    assert torch.equal(again, out)  # the cluster reduction is deterministic
+    g = tq.lora_grad(x, out_t, 0)
+    g_ref = (x.float().t() @ out_t[:, :m].float().t()).cpu().numpy()
+    err = oracle.rel_err(g.cpu().numpy(), g_ref)
+    assert err <= 1e-4, f"grad: max rel err {err:.3e}"

@@ -306,6 +306,24 @@ __device__ __forceinline__ void cluster_sync() {
       "barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
 }
 
+// Split form of cluster_sync: arrive early (no ordering), wait later.  Every
+// thread of every CTA of the cluster executes both, in this order.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// 16-byte store into the shared memory of a CTA of the cluster (caddr from
+// mapa_shared); made visible to that CTA by a later cluster_sync.
+__device__ __forceinline__ void st_cluster_v4(uint32_t caddr, uint32_t a, uint32_t b, uint32_t c,
+                                              uint32_t d) {
+  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(caddr), "r"(a), "r"(b),
+               "r"(c), "r"(d)
+               : "memory");
+}
+
 // One arrival on an mbarrier of either CTA (cbar: shared::cluster address).
 // Default semantics (release at CTA scope), as for a local arrive: a
 // cluster-scope release here stalls the arriving warp on a memory barrier
