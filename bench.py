@@ -63,7 +63,10 @@ def parse_args():
     p.add_argument("--n", type=int, default=4096, help="qmm: weight rows (out features)")
     p.add_argument("--k", type=int, default=4096, help="qmm: weight cols (in features)")
     p.add_argument("--direction", choices=("fwd", "dx"), default="fwd")
-    p.add_argument("--bits", type=int, choices=(4, 8), default=4, help="qmm: code width")
+    p.add_argument("--bits", type=int, choices=(4, 8), default=None,
+                   help="qmm: code width (default 4); quant-sweep: only this width")
+    p.add_argument("--group", type=int, choices=(32, 64, 128), default=None,
+                   help="quant-sweep: only this group size")
     p.add_argument("--global-batch", type=int, default=None)
     p.add_argument("--seq", type=int, default=None)
     p.add_argument("--micro-batch", type=int, default=None)
@@ -488,7 +491,8 @@ def run_kernels(args):
     common = {"n_gpus": 1, "steps": K, "warmup": W, "higher_is_better": True,
               "vs_baseline": None, "data": "synthetic"}
     if args.workload == "qmm":
-        fn, _ = _qmm_case(args.m, args.n, args.k, args.direction, dev, bits=args.bits)
+        bits = args.bits or 4
+        fn, _ = _qmm_case(args.m, args.n, args.k, args.direction, dev, bits=bits)
         ms = _time_kernel(fn, K, W, flush)
         tf = 2.0 * args.m * args.n * args.k / (ms / 1000.0) / 1e12
         print(json.dumps({"metric": "int4 quantized_matmul TFLOP/s", "value": tf,
@@ -496,7 +500,7 @@ def run_kernels(args):
                           "dtype": "bf16", **common,
                           "config": {"workload": f"quantized_matmul {args.direction}",
                                      "m": args.m, "w_rows": args.n, "w_cols": args.k,
-                                     "bits": args.bits, "group_size": 64,
+                                     "bits": bits, "group_size": 64,
                                      "l2": "flushed before every launch (clean)"},
                           "roofline": {"bound": "tensor", "achieved": tf, "peak": burst,
                                        "unit": "TFLOP/s", "frac": tf / burst,
@@ -546,8 +550,8 @@ def run_kernels(args):
         # Each shape stacked over the 24 layers, so a launch is HBM-sized.
         big = [torch.cat([wm] * QWEN2_5_0_5B.layers) for wm in mats]
         rows = []
-        for bits in (4, 8):
-            for grp in (32, 64, 128):
+        for bits in (4, 8) if args.bits is None else (args.bits,):
+            for grp in (32, 64, 128) if args.group is None else (args.group,):
                 tq_ms = tdq_ms = 0.0
                 nbytes = 0.0
                 for wm in big:

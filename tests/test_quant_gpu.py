@@ -61,6 +61,10 @@ def _edge_matrix(oracle, cols):
     r = np.linspace(-1.0, 1.0, cols, dtype=f); r[7] = -np.inf; rows.append(r)  # -inf
     r = np.zeros(cols, f); r[::2] = -0.0; r[1] = 1e-3; rows.append(r)          # signed zeros
     r = np.linspace(1.0, 1.0001, cols, dtype=f); rows.append(r)     # nearly constant: huge q0
+    rows.append(np.full(cols, np.nan, f))                           # all NaN
+    r = -np.abs(np.linspace(0.1, 2.0, cols, dtype=f))
+    r[::3] = 0.0; r[1::3] = -0.0; rows.append(r)                    # zeros of both signs as max
+    r = np.linspace(-1.0, 1.0, cols, dtype=f); r[::4] = np.nan; rows.append(r)  # NaN-riddled
     return oracle.bf16_from_f32(np.stack(rows))
 
 

@@ -19,6 +19,18 @@ __device__ __forceinline__ float mlx_min(float a, float b) { return b < a ? b : 
 
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t h) { return __uint_as_float(h << 16); }
 
+// Lane-wise max / min of two bf16 pairs; a NaN lane yields the other operand.
+__device__ __forceinline__ uint32_t bf16x2_max(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf16x2_min(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("min.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 // f32 -> bf16 bits, round to nearest even (NaN -> canonical quiet NaN 0x7FC0).
 __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
   if (f != f) return 0x7FC0;
@@ -49,20 +61,19 @@ __device__ __forceinline__ void quantize_run(const uint4 (&r)[4], bool live, int
     words[4 * k + 2] = r[k].z;
     words[4 * k + 3] = r[k].w;
   }
-  float v[kE];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    v[2 * j] = bf16_bits_to_f32(words[j] & 0xFFFFu);
-    v[2 * j + 1] = bf16_bits_to_f32(words[j] >> 16);
-  }
-  float w_max = -INFINITY, w_min = INFINITY;
+  // Group max/min on bf16 pairs: exact (the result is one of the inputs), a
+  // NaN element is passed over as the f32 comparisons of the oracle do, and
+  // the sign of a zero extreme cannot change the scale or bias below.
+  uint32_t mx2 = 0xFF80FF80u, mn2 = 0x7F807F80u;  // (-inf, -inf), (+inf, +inf)
   if (live) {
 #pragma unroll
-    for (int j = 0; j < kE; ++j) {
-      w_max = mlx_max(w_max, v[j]);
-      w_min = mlx_min(w_min, v[j]);
+    for (int j = 0; j < 16; ++j) {
+      mx2 = bf16x2_max(mx2, words[j]);
+      mn2 = bf16x2_min(mn2, words[j]);
     }
   }
+  float w_max = fmaxf(bf16_bits_to_f32(mx2 & 0xFFFFu), bf16_bits_to_f32(mx2 >> 16));
+  float w_min = fminf(bf16_bits_to_f32(mn2 & 0xFFFFu), bf16_bits_to_f32(mn2 >> 16));
 #pragma unroll
   for (int off = 1; off < LANES; off <<= 1) {
     w_max = mlx_max(w_max, __shfl_xor_sync(0xffffffffu, w_max, off));
@@ -86,25 +97,28 @@ __device__ __forceinline__ void quantize_run(const uint4 (&r)[4], bool live, int
   // of the quotient itself decides), is not finite, or is that large.  Of
   // those, an exact quotient (d - y * scale == 0 by one fma, d normal) is y
   // itself; the rest, about 0.05-0.2 % of elements, take the IEEE division.
+  // The code is the quotient converted with round-to-nearest-even and
+  // saturation (negatives and NaN give 0), then capped at 2^bits - 1: the
+  // clamp of rint(q) to [0, 2^bits - 1] in two integer steps.
   const float rs = __frcp_rn(scale);
   uint32_t packed[BITS] = {};  // 32 codes: 4 words at 4 bits, 8 at 8
 #pragma unroll
   for (int j = 0; j < kE; ++j) {
-    const float d = __fsub_rn(v[j], bias);
+    const uint32_t h = words[j >> 1];
+    const float vj = (j & 1) ? __uint_as_float(h & 0xFFFF0000u) : __uint_as_float(h << 16);
+    const float d = __fsub_rn(vj, bias);
     const float y = __fmul_rn(d, rs);
-    float q = rintf(y);
-    const float margin = 0.5f - fabsf(__fsub_rn(y, q));
-    if (!(margin > 0x1p-12f) || !(fabsf(y) < 512.0f)) {
+    float yq = y;
+    if (!(fabsf(__fsub_rn(y, rintf(y))) < 0.5f - 0x1p-12f) || !(fabsf(y) < 512.0f)) {
       const bool exact = fabsf(y) < 512.0f && fabsf(d) > 0x1p-100f &&
                          __fmaf_rn(-y, scale, d) == 0.0f;
-      if (!exact) q = rintf(__fdiv_rn(d, scale));
+      if (!exact) yq = __fdiv_rn(d, scale);
     }
-    q = mlx_min(mlx_max(q, 0.0f), n_bins);
-    const uint32_t code = (q == q) ? static_cast<uint32_t>(q) : 0u;
+    const uint32_t code = min(__float2uint_rn(yq), (1u << BITS) - 1u);
     if constexpr (BITS == 4) {
-      packed[j >> 3] |= code << (4 * (j & 7));
+      packed[j >> 3] += code << (4 * (j & 7));
     } else {
-      packed[j >> 2] |= code << (8 * (j & 3));
+      packed[j >> 2] += code << (8 * (j & 3));
     }
   }
   if (live) {
