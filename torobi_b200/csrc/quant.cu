@@ -47,6 +47,7 @@ __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
 // times the elements of one vector a thread.
 template <int BITS, int LANES>
 __device__ __forceinline__ void quantize_run(const uint4 (&r)[4], bool live, int64_t pi,
+                                             const uint16_t* __restrict__ src,
                                              int lane, uint32_t* __restrict__ codes,
                                              uint16_t* __restrict__ scales,
                                              uint16_t* __restrict__ biases) {
@@ -97,27 +98,73 @@ __device__ __forceinline__ void quantize_run(const uint4 (&r)[4], bool live, int
   // of the quotient itself decides), is not finite, or is that large.  Of
   // those, an exact quotient (d - y * scale == 0 by one fma, d normal) is y
   // itself; the rest, about 0.05-0.2 % of elements, take the IEEE division.
-  // The code is the quotient converted with round-to-nearest-even and
-  // saturation (negatives and NaN give 0), then capped at 2^bits - 1: the
-  // clamp of rint(q) to [0, 2^bits - 1] in two integer steps.
+  //
+  // |y| < 512 holds for every element of the group when it holds for the
+  // largest |d| (rounding is monotone, so no element's y exceeds
+  // fl(max|d| * |rs|)); one test a group replaces one an element.  Groups
+  // with an infinite or NaN extreme, or a huge q0, fail it and take the
+  // exact path throughout.
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  constexpr int kMaxCode = (1 << BITS) - 1;
   const float rs = __frcp_rn(scale);
+  const float d_top = fmaxf(fabsf(__fsub_rn(w_max, bias)), fabsf(__fsub_rn(w_min, bias)));
+  const bool in_range = __fmul_rn(d_top, fabsf(rs)) < 512.0f;
   uint32_t packed[BITS] = {};  // 32 codes: 4 words at 4 bits, 8 at 8
+  if constexpr (BITS == 4) {
+    // Without a branch or a conversion instruction: t = y + 1.5 * 2^23
+    // rounds y to an integer (ties to even, |y| < 2^22), so t - 1.5 * 2^23
+    // is rint(y) and t's low mantissa bits are that integer; the code is it
+    // clamped to [0, 15].  Elements needing more are marked in `fix` and
+    // redone after the loop from their bf16 value (an L1 hit).
+    uint32_t fix = 0;
 #pragma unroll
-  for (int j = 0; j < kE; ++j) {
-    const uint32_t h = words[j >> 1];
-    const float vj = (j & 1) ? __uint_as_float(h & 0xFFFF0000u) : __uint_as_float(h << 16);
-    const float d = __fsub_rn(vj, bias);
-    const float y = __fmul_rn(d, rs);
-    float yq = y;
-    if (!(fabsf(__fsub_rn(y, rintf(y))) < 0.5f - 0x1p-12f) || !(fabsf(y) < 512.0f)) {
-      const bool exact = fabsf(y) < 512.0f && fabsf(d) > 0x1p-100f &&
-                         __fmaf_rn(-y, scale, d) == 0.0f;
-      if (!exact) yq = __fdiv_rn(d, scale);
+    for (int j = 0; j < kE; ++j) {
+      const uint32_t h = words[j >> 1];
+      const float vj = (j & 1) ? __uint_as_float(h & 0xFFFF0000u) : __uint_as_float(h << 16);
+      const float d = __fsub_rn(vj, bias);
+      const float y = __fmul_rn(d, rs);
+      const float t = __fadd_rn(y, kRound);
+      const float q = __fsub_rn(t, kRound);
+      if (!(fabsf(__fsub_rn(y, q)) < 0.5f - 0x1p-12f)) fix |= 1u << j;
+      const int qi = static_cast<int>(__float_as_uint(t) - __float_as_uint(kRound));
+      packed[j >> 3] += static_cast<uint32_t>(__vimin_s32_relu(qi, kMaxCode)) << (4 * (j & 7));
     }
-    const uint32_t code = min(__float2uint_rn(yq), (1u << BITS) - 1u);
-    if constexpr (BITS == 4) {
-      packed[j >> 3] += code << (4 * (j & 7));
-    } else {
+    if (!in_range) fix = 0xFFFFFFFFu;
+    if (!live) fix = 0;  // src is only valid for a live run
+    while (fix) {
+      const int j = __ffs(fix) - 1;
+      fix &= fix - 1;
+      const float vj = bf16_bits_to_f32(__ldg(src + j));
+      const float d = __fsub_rn(vj, bias);
+      const float y = __fmul_rn(d, rs);
+      const bool exact =
+          fabsf(y) < 512.0f && fabsf(d) > 0x1p-100f && __fmaf_rn(-y, scale, d) == 0.0f;
+      const float yq = exact ? y : __fdiv_rn(d, scale);
+      const uint32_t code = min(__float2uint_rn(yq), static_cast<uint32_t>(kMaxCode));
+      const int sh = 4 * (j & 7);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (k == (j >> 3)) packed[k] = (packed[k] & ~(15u << sh)) | (code << sh);
+    }
+  } else {
+    // At 8 bits the bf16 grid often puts quotients exactly on half-integers
+    // (about one code per representable value), so the exceptions are
+    // handled in line: a deferred pass over them ran 13-19 % slower here.
+    // The code is the quotient converted with round-to-nearest-even and
+    // saturation (negatives and NaN give 0), capped at 255.
+#pragma unroll
+    for (int j = 0; j < kE; ++j) {
+      const uint32_t h = words[j >> 1];
+      const float vj = (j & 1) ? __uint_as_float(h & 0xFFFF0000u) : __uint_as_float(h << 16);
+      const float d = __fsub_rn(vj, bias);
+      const float y = __fmul_rn(d, rs);
+      float yq = y;
+      if (!(fabsf(__fsub_rn(y, rintf(y))) < 0.5f - 0x1p-12f) || !in_range) {
+        const bool exact = fabsf(y) < 512.0f && fabsf(d) > 0x1p-100f &&
+                           __fmaf_rn(-y, scale, d) == 0.0f;
+        if (!exact) yq = __fdiv_rn(d, scale);
+      }
+      const uint32_t code = min(__float2uint_rn(yq), static_cast<uint32_t>(kMaxCode));
       packed[j >> 2] += code << (8 * (j & 3));
     }
   }
@@ -149,7 +196,8 @@ __global__ void __launch_bounds__(256) quantize_kernel(const uint4* __restrict__
     uint4 r[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) r[k] = live ? __ldg(w + 4 * pi + k) : make_uint4(0, 0, 0, 0);
-    quantize_run<BITS, LANES>(r, live, pi, lane, codes, scales, biases);
+    quantize_run<BITS, LANES>(r, live, pi, reinterpret_cast<const uint16_t*>(w + 4 * pi), lane,
+                              codes, scales, biases);
   }
 }
 
