@@ -467,6 +467,43 @@ def _qmm_case(m, n, k, direction, dev, seed=0, bits=4):
     return (lambda: ops.quantized_matmul(dy, c, s, b, False, 64, bits)), (dy, c, s, b)
 
 
+def _grouped_quant_ms(stacks, layers, grp, bits, K, W, flush):
+    """CUDA-event ms of one tq_quantize_batch and one tq_dequantize_batch over
+    every layer's matrix of every stacked shape (len(stacks) * layers jobs)."""
+    import torch
+
+    from torobi_b200._lib import TqDequantizeJob, TqQuantizeJob, lib
+
+    mats = [st[l * (st.shape[0] // layers):(l + 1) * (st.shape[0] // layers)]
+            for st in stacks for l in range(layers)]
+    n = len(mats)
+    qjobs, djobs = (TqQuantizeJob * n)(), (TqDequantizeJob * n)()
+    keep = []
+    for i, w in enumerate(mats):
+        r, c = w.shape
+        codes = torch.empty(r, c * bits // 32, dtype=torch.uint32, device=w.device)
+        sc = torch.empty(r, c // grp, dtype=torch.bfloat16, device=w.device)
+        bi = torch.empty_like(sc)
+        out = torch.empty_like(w)
+        keep += [codes, sc, bi, out]
+        qjobs[i] = TqQuantizeJob(w.data_ptr(), r, c, codes.data_ptr(), sc.data_ptr(), bi.data_ptr())
+        djobs[i] = TqDequantizeJob(codes.data_ptr(), sc.data_ptr(), bi.data_ptr(), r, c,
+                                   out.data_ptr())
+    L = lib()
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def q():
+        assert L.tq_quantize_batch(qjobs, n, grp, bits, stream) == 0
+
+    def dq():
+        assert L.tq_dequantize_batch(djobs, n, grp, bits, stream) == 0
+
+    gq = _time_kernel(q, K, W, flush)
+    gdq = _time_kernel(dq, K, W, flush)
+    del keep
+    return gq, gdq
+
+
 def run_kernels(args):
     import torch
 
@@ -560,8 +597,15 @@ def run_kernels(args):
                     tdq_ms += _time_kernel(lambda: ops.dequantize(c, s_, b_, grp, bits), K, W,
                                            flush)
                     nbytes += wm.numel() * (2 + bits / 8 + 4 / grp)
+                # The same bytes as one grouped launch over the 168 matrices
+                # (each shape's 24 layers as separate [rows, cols] views), the
+                # job tables built before the timed region.
+                gq_ms, gdq_ms = _grouped_quant_ms(big, QWEN2_5_0_5B.layers, grp, bits, K, W,
+                                                  flush)
                 rows.append({"bits": bits, "group": grp, "quantize_gbs": nbytes / tq_ms / 1e6,
-                             "dequantize_gbs": nbytes / tdq_ms / 1e6, "bytes": nbytes})
+                             "dequantize_gbs": nbytes / tdq_ms / 1e6,
+                             "grouped_quantize_gbs": nbytes / gq_ms / 1e6,
+                             "grouped_dequantize_gbs": nbytes / gdq_ms / 1e6, "bytes": nbytes})
                 print(json.dumps(rows[-1]), file=sys.stderr, flush=True)
         val = sum(r["dequantize_gbs"] for r in rows) / len(rows)
         print(json.dumps({"metric": "quantize/dequantize GB/s (Qwen2.5-0.5B shapes, 24 layers)",

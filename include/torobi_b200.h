@@ -89,6 +89,35 @@ int tq_quantize(const void* w, int64_t rows, int64_t cols, int group_size, int b
 int tq_dequantize(const void* codes, const void* scales, const void* biases, int64_t rows,
                   int64_t cols, int group_size, int bits, void* w, void* stream);
 
+/*
+ * Many matrices in one launch (every linear of a model at load time): job i
+ * is tq_quantize's / tq_dequantize's arguments for one matrix, with one
+ * group_size and bits for all.  Every job is checked before anything is
+ * launched (errors name the job); empty jobs are skipped; more than 256
+ * non-empty jobs take one launch per 256.  No counterpart in the reference
+ * (quantize is not bound there); the batched form of the two above.
+ */
+typedef struct {
+  const void* w; /* bf16 [rows, cols] */
+  int64_t rows, cols;
+  void* codes;   /* u32 [rows, cols * bits / 32] */
+  void* scales;  /* bf16 [rows, cols / group_size] */
+  void* biases;  /* bf16 [rows, cols / group_size] */
+} TqQuantizeJob;
+
+typedef struct {
+  const void* codes;
+  const void* scales;
+  const void* biases;
+  int64_t rows, cols;
+  void* w; /* bf16 [rows, cols] out */
+} TqDequantizeJob;
+
+int tq_quantize_batch(const TqQuantizeJob* jobs, int n_jobs, int group_size, int bits,
+                      void* stream);
+int tq_dequantize_batch(const TqDequantizeJob* jobs, int n_jobs, int group_size, int bits,
+                        void* stream);
+
 /* ----------------------------------------------------------- the GEMM ---- */
 
 /*

@@ -155,3 +155,57 @@ def test_quantize_errors_and_empty(cuda):
     assert c.shape == (0, 8) and s.shape == (0, 1) and b.shape == (0, 1)
     d = tq.dequantize(c, s, b, 64, 4)
     assert d.shape == (0, 64)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bits,group", [(4, 64), (8, 32), (4, 128)])
+def test_batched_quantize_and_dequantize_match_the_oracle(cuda, oracle, bits, group):
+    """One launch over matrices of every Qwen2.5-0.5B-shaped linear plus
+    ragged, tiny and empty ones, bit-exact to the oracle per matrix; more
+    than 256 matrices take several launches with the same results."""
+    import torch
+    import torobi_b200 as tq
+
+    rng = np.random.default_rng(7)
+    shapes = list(QWEN_SHAPES.values()) + [(3, group), (1, 4 * group), (0, group), (37, 2 * group)]
+    ws = [oracle.normal_bf16(rng, s, 0.02) for s in shapes]
+    ws[2][5, : 2 * group] = oracle.bf16_from_f32(np.full(2 * group, np.nan, np.float32))
+    got = tq.quantize_batch([dev_bf16(w, cuda) for w in ws], group, bits)
+    deq = tq.dequantize_batch(got, group, bits)
+    for i, (w, (c, s_, b_), d) in enumerate(zip(ws, got, deq)):
+        codes, scales, biases = oracle.quantize(w, bits, group)
+        assert np.array_equal(host_u32(c), codes), (i, first_mismatch(host_u32(c), codes))
+        assert bf16_equal(host_bf16(s_), scales) and bf16_equal(host_bf16(b_), biases), i
+        assert bf16_equal(host_bf16(d), oracle.dequantize(codes, scales, biases, bits, group)), i
+    many = [dev_bf16(oracle.normal_bf16(rng, (2 + i % 5, group), 0.1), cuda) for i in range(300)]
+    batched = tq.quantize_batch(many, group, bits)
+    for w, (c, s_, b_) in zip(many, batched):
+        c1, s1, b1 = tq.quantize(w, group, bits)
+        assert torch.equal(c, c1) and torch.equal(s_.view(torch.int16), s1.view(torch.int16))
+        assert torch.equal(b_.view(torch.int16), b1.view(torch.int16))
+    back = tq.dequantize_batch(batched, group, bits)
+    for (c, s_, b_), d in zip(batched, back):
+        assert torch.equal(d.view(torch.int16), tq.dequantize(c, s_, b_, group, bits).view(torch.int16))
+    assert tq.quantize_batch([], group, bits) == []
+
+
+@pytest.mark.gpu
+def test_batched_quantize_refuses_a_bad_job_before_launching(cuda):
+    import ctypes
+
+    import torch
+    import torobi_b200 as tq
+    from torobi_b200._lib import TQ_ERR_INVALID, TqQuantizeJob, lib
+
+    w = torch.zeros(4, 64, dtype=torch.bfloat16, device=cuda)
+    codes = torch.full((4, 8), 7, dtype=torch.uint32, device=cuda)
+    sb = torch.zeros(4, 1, dtype=torch.bfloat16, device=cuda)
+    jobs = (TqQuantizeJob * 2)(
+        TqQuantizeJob(w.data_ptr(), 4, 64, codes.data_ptr(), sb.data_ptr(), sb.data_ptr()),
+        TqQuantizeJob(w.data_ptr(), 4, 48, codes.data_ptr(), sb.data_ptr(), sb.data_ptr()))
+    assert lib().tq_quantize_batch(jobs, 2, 64, 4, None) == TQ_ERR_INVALID
+    assert b"job 1" in lib().tq_last_error()
+    torch.cuda.synchronize()
+    assert int(codes[0, 0]) == 7  # nothing ran
+    with pytest.raises(ValueError):
+        tq.quantize_batch([w, w[:, :48]], 64, 4)

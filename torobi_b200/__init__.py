@@ -4,11 +4,11 @@ LoRA branch fused into its tensor-memory accumulator, and the data-parallel
 LoRA step -- behind the C ABI of include/torobi_b200.h.
 """
 from ._lib import LIB_PATH, TqError, device_status, header_symbols, lib
-from .ops import (adamw_, dequantize, lora_down, lora_grad, qlora_matmul, quantize,
-                  quantized_matmul, sumsq, transpose_to_bf16)
+from .ops import (adamw_, dequantize, dequantize_batch, lora_down, lora_grad, qlora_matmul,
+                  quantize, quantize_batch, quantized_matmul, sumsq, transpose_to_bf16)
 
 __all__ = [
     "LIB_PATH", "TqError", "device_status", "header_symbols", "lib", "adamw_", "dequantize",
-    "lora_down", "lora_grad", "qlora_matmul", "quantize", "quantized_matmul", "sumsq",
-    "transpose_to_bf16",
+    "dequantize_batch", "lora_down", "lora_grad", "qlora_matmul", "quantize", "quantize_batch",
+    "quantized_matmul", "sumsq", "transpose_to_bf16",
 ]

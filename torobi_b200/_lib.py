@@ -47,11 +47,25 @@ _i32 = ctypes.c_int
 _f32 = ctypes.c_float
 
 # Argument types of every entry point, in header order.
+class TqQuantizeJob(ctypes.Structure):
+    """One matrix of tq_quantize_batch (the header's TqQuantizeJob)."""
+    _fields_ = [("w", _vp), ("rows", _i64), ("cols", _i64), ("codes", _vp), ("scales", _vp),
+                ("biases", _vp)]
+
+
+class TqDequantizeJob(ctypes.Structure):
+    """One matrix of tq_dequantize_batch (the header's TqDequantizeJob)."""
+    _fields_ = [("codes", _vp), ("scales", _vp), ("biases", _vp), ("rows", _i64), ("cols", _i64),
+                ("w", _vp)]
+
+
 SIGNATURES = {
     "tq_version": ([], _i32),
     "tq_last_error": ([], ctypes.c_char_p),
     "tq_device_status": ([ctypes.POINTER(_i32), _i32], _i32),
     "tq_wait_selftest": ([_i64, _vp], _i32),
+    "tq_quantize_batch": ([ctypes.POINTER(TqQuantizeJob), _i32, _i32, _i32, _vp], _i32),
+    "tq_dequantize_batch": ([ctypes.POINTER(TqDequantizeJob), _i32, _i32, _i32, _vp], _i32),
     "tq_quantize": ([_vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _vp], _i32),
     "tq_dequantize": ([_vp, _vp, _vp, _i64, _i64, _i32, _i32, _vp, _vp], _i32),
     "tq_quantized_matmul": ([_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _i32, _vp, _vp],

@@ -8,6 +8,8 @@
 // a whole number of groups for group_size in {32, 64, 128}).
 #include <cuda_bf16.h>
 
+#include <cstdio>
+
 #include "tq_ptx.cuh"
 #include "tq_runtime.h"
 
@@ -207,43 +209,130 @@ __global__ void __launch_bounds__(256) quantize_kernel(const uint4* __restrict__
 // their groups' scale and bias) before any is dequantized.
 constexpr int kWords = 8;
 
+// One warp-span of kWords * 32 words starting at `base`: lane `lane` takes
+// words base + 32k + lane, all loaded (with their groups' scale and bias)
+// before any is dequantized.
+template <int BITS>
+__device__ __forceinline__ void dequantize_span(const uint32_t* __restrict__ codes,
+                                                int64_t n_words, int64_t base, int lane,
+                                                int group_shift,
+                                                const uint16_t* __restrict__ scales,
+                                                const uint16_t* __restrict__ biases,
+                                                uint16_t* __restrict__ out) {
+  constexpr int kElems = 32 / BITS;  // elements per word
+  uint32_t c[kWords], s2[kWords], b2[kWords];
+#pragma unroll
+  for (int k = 0; k < kWords; ++k) {
+    const int64_t wi = base + 32 * k + lane;
+    const bool live = wi < n_words;
+    c[k] = live ? __ldg(codes + wi) : 0u;
+    const int64_t gi = live ? (wi * kElems) >> group_shift : 0;  // a group never straddles a word
+    s2[k] = bf16_dup(__ldg(scales + gi));
+    b2[k] = bf16_dup(__ldg(biases + gi));
+  }
+#pragma unroll
+  for (int k = 0; k < kWords; ++k) {
+    const int64_t wi = base + 32 * k + lane;
+    if (wi >= n_words) break;
+    if constexpr (BITS == 4) {
+      uint32_t o[4];
+      dequant_u4x8(c[k], s2[k], b2[k], o);
+      reinterpret_cast<uint4*>(out)[wi] = make_uint4(o[0], o[1], o[2], o[3]);
+    } else {
+      uint32_t o[2];
+      dequant_u8x4(c[k], s2[k], b2[k], o);
+      reinterpret_cast<uint2*>(out)[wi] = make_uint2(o[0], o[1]);
+    }
+  }
+}
+
 template <int BITS>
 __global__ void __launch_bounds__(256) dequantize_kernel(const uint32_t* __restrict__ codes,
                                                          int64_t n_words, int group_shift,
                                                          const uint16_t* __restrict__ scales,
                                                          const uint16_t* __restrict__ biases,
                                                          uint16_t* __restrict__ out) {
-  constexpr int kElems = 32 / BITS;  // elements per word
   const int lane = threadIdx.x & 31;
   const int64_t span = 32 * kWords;  // words a warp covers per iteration
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   for (int64_t base = (static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) *
                       span;
-       base < n_words; base += warps * span) {
-    uint32_t c[kWords], s2[kWords], b2[kWords];
+       base < n_words; base += warps * span)
+    dequantize_span<BITS>(codes, n_words, base, lane, group_shift, scales, biases, out);
+}
+
+// ------------------------------------------------------------- batches ----
+//
+// Many matrices in one launch (every linear of a model at load time).  Each
+// job's work is laid out in a virtual index space padded to whole warp
+// iterations (32 runs for quantize, one span of words for dequantize), so a
+// warp finds its job once per iteration by a binary search over the starts
+// and never straddles two; the tables travel as a kernel parameter.
+constexpr int kBatchMax = 256;  // tables of about 12 KB, within the 32 KB of kernel parameters
+
+struct QuantizeBatch {
+  int n;
+  int64_t start[kBatchMax + 1];  // virtual run index of each job's first run; start[n] = end
+  int64_t runs[kBatchMax];
+  const uint4* w[kBatchMax];
+  uint32_t* codes[kBatchMax];
+  uint16_t* scales[kBatchMax];
+  uint16_t* biases[kBatchMax];
+};
+
+struct DequantizeBatch {
+  int n;
+  int64_t start[kBatchMax + 1];  // virtual word index of each job's first word
+  int64_t words[kBatchMax];
+  const uint32_t* codes[kBatchMax];
+  const uint16_t* scales[kBatchMax];
+  const uint16_t* biases[kBatchMax];
+  uint16_t* out[kBatchMax];
+};
+
+// The last job whose start is <= v (starts ascending, start[0] = 0).
+__device__ __forceinline__ int find_job(const int64_t* start, int n, int64_t v) {
+  int lo = 0, hi = n - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (start[mid] <= v) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+template <int BITS, int LANES>
+__global__ void __launch_bounds__(256) quantize_batch_kernel(const __grid_constant__ QuantizeBatch b) {
+  const int lane = threadIdx.x & 31;
+  const int64_t end = b.start[b.n];
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31);
+       base < end; base += stride) {
+    const int j = find_job(b.start, b.n, base);
+    const int64_t pi = base - b.start[j] + lane;
+    const bool live = pi < b.runs[j];
+    const uint4* w = b.w[j];
+    uint4 r[4];
 #pragma unroll
-    for (int k = 0; k < kWords; ++k) {
-      const int64_t wi = base + 32 * k + lane;
-      const bool live = wi < n_words;
-      c[k] = live ? __ldg(codes + wi) : 0u;
-      const int64_t gi = live ? (wi * kElems) >> group_shift : 0;  // a group never straddles a word
-      s2[k] = bf16_dup(__ldg(scales + gi));
-      b2[k] = bf16_dup(__ldg(biases + gi));
-    }
-#pragma unroll
-    for (int k = 0; k < kWords; ++k) {
-      const int64_t wi = base + 32 * k + lane;
-      if (wi >= n_words) break;
-      if constexpr (BITS == 4) {
-        uint32_t o[4];
-        dequant_u4x8(c[k], s2[k], b2[k], o);
-        reinterpret_cast<uint4*>(out)[wi] = make_uint4(o[0], o[1], o[2], o[3]);
-      } else {
-        uint32_t o[2];
-        dequant_u8x4(c[k], s2[k], b2[k], o);
-        reinterpret_cast<uint2*>(out)[wi] = make_uint2(o[0], o[1]);
-      }
-    }
+    for (int k = 0; k < 4; ++k) r[k] = live ? __ldg(w + 4 * pi + k) : make_uint4(0, 0, 0, 0);
+    quantize_run<BITS, LANES>(r, live, pi, reinterpret_cast<const uint16_t*>(w + 4 * pi), lane,
+                              b.codes[j], b.scales[j], b.biases[j]);
+  }
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(256) dequantize_batch_kernel(const __grid_constant__ DequantizeBatch b,
+                                                               int group_shift) {
+  const int lane = threadIdx.x & 31;
+  const int64_t span = 32 * kWords;
+  const int64_t end = b.start[b.n];
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t base = (static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) *
+                      span;
+       base < end; base += warps * span) {
+    const int j = find_job(b.start, b.n, base);
+    dequantize_span<BITS>(b.codes[j], b.words[j], base - b.start[j], lane, group_shift,
+                          b.scales[j], b.biases[j], b.out[j]);
   }
 }
 
@@ -325,4 +414,125 @@ extern "C" int tq_dequantize(const void* codes, const void* scales, const void* 
   else
     dequantize_kernel<8><<<grid, block, 0, s>>>(cw, n_words, shift, sp, bp, op);
   return check_cuda(cudaGetLastError(), "dequantize launch");
+}
+
+namespace {
+
+// The per-matrix checks of tq_quantize / tq_dequantize, for job `i`.
+int check_job(int64_t i, const void* in, int64_t rows, int64_t cols, const void* codes,
+              const void* scales, const void* biases, int group_size, int bits, bool quantize) {
+  using namespace tq;
+  int rc = check_qargs(rows, cols, group_size, bits);
+  if (rc) {
+    char msg[256];
+    snprintf(msg, sizeof msg, "%s", tq_last_error());  // fail() rewrites that buffer
+    return fail(rc, "job %lld: %s", static_cast<long long>(i), msg);
+  }
+  if (rows == 0 || cols == 0) return TQ_OK;
+  if (!in || !codes || !scales || !biases)
+    return fail(TQ_ERR_INVALID, "job %lld: null pointer", static_cast<long long>(i));
+  if (!aligned(in, 16) || !aligned(codes, 16))
+    return fail(TQ_ERR_MISALIGNED, "job %lld: %s and codes must be 16-byte aligned",
+                static_cast<long long>(i), quantize ? "w" : "out");
+  if (!aligned(scales, 2) || !aligned(biases, 2))
+    return fail(TQ_ERR_MISALIGNED, "job %lld: scales and biases must be 2-byte aligned",
+                static_cast<long long>(i));
+  return TQ_OK;
+}
+
+}  // namespace
+
+extern "C" int tq_quantize_batch(const TqQuantizeJob* jobs, int n_jobs, int group_size, int bits,
+                                 void* stream) {
+  using namespace tq;
+  if (n_jobs < 0 || (n_jobs > 0 && !jobs)) return fail(TQ_ERR_INVALID, "quantize_batch: bad job list");
+  int rc = check_qargs(0, group_size, group_size, bits);
+  if (rc) return rc;
+  for (int i = 0; i < n_jobs; ++i) {
+    const TqQuantizeJob& j = jobs[i];
+    rc = check_job(i, j.w, j.rows, j.cols, j.codes, j.scales, j.biases, group_size, bits, true);
+    if (rc) return rc;
+  }
+  cudaStream_t s = as_stream(stream);
+  const int lanes = group_size / 32;
+  QuantizeBatch b;
+  int i = 0;
+  while (i < n_jobs) {
+    b.n = 0;
+    int64_t v = 0;
+    for (; i < n_jobs && b.n < kBatchMax; ++i) {
+      const TqQuantizeJob& j = jobs[i];
+      const int64_t runs = j.rows * j.cols / 32;
+      if (runs == 0) continue;
+      b.start[b.n] = v;
+      b.runs[b.n] = runs;
+      b.w[b.n] = static_cast<const uint4*>(j.w);
+      b.codes[b.n] = static_cast<uint32_t*>(j.codes);
+      b.scales[b.n] = static_cast<uint16_t*>(j.scales);
+      b.biases[b.n] = static_cast<uint16_t*>(j.biases);
+      v += (runs + 31) / 32 * 32;  // whole warp iterations
+      ++b.n;
+    }
+    if (b.n == 0) break;
+    b.start[b.n] = v;
+    const int grid = grid_for(v, 256);
+    if (bits == 4) {
+      if (lanes == 1) quantize_batch_kernel<4, 1><<<grid, 256, 0, s>>>(b);
+      else if (lanes == 2) quantize_batch_kernel<4, 2><<<grid, 256, 0, s>>>(b);
+      else quantize_batch_kernel<4, 4><<<grid, 256, 0, s>>>(b);
+    } else {
+      if (lanes == 1) quantize_batch_kernel<8, 1><<<grid, 256, 0, s>>>(b);
+      else if (lanes == 2) quantize_batch_kernel<8, 2><<<grid, 256, 0, s>>>(b);
+      else quantize_batch_kernel<8, 4><<<grid, 256, 0, s>>>(b);
+    }
+    rc = check_cuda(cudaGetLastError(), "quantize_batch launch");
+    if (rc) return rc;
+  }
+  return TQ_OK;
+}
+
+extern "C" int tq_dequantize_batch(const TqDequantizeJob* jobs, int n_jobs, int group_size,
+                                   int bits, void* stream) {
+  using namespace tq;
+  if (n_jobs < 0 || (n_jobs > 0 && !jobs))
+    return fail(TQ_ERR_INVALID, "dequantize_batch: bad job list");
+  int rc = check_qargs(0, group_size, group_size, bits);
+  if (rc) return rc;
+  for (int i = 0; i < n_jobs; ++i) {
+    const TqDequantizeJob& j = jobs[i];
+    rc = check_job(i, j.w, j.rows, j.cols, j.codes, j.scales, j.biases, group_size, bits, false);
+    if (rc) return rc;
+  }
+  cudaStream_t s = as_stream(stream);
+  const int shift = group_size == 32 ? 5 : (group_size == 64 ? 6 : 7);
+  constexpr int64_t kSpan = 32 * kWords;
+  DequantizeBatch b;
+  int i = 0;
+  while (i < n_jobs) {
+    b.n = 0;
+    int64_t v = 0;
+    for (; i < n_jobs && b.n < kBatchMax; ++i) {
+      const TqDequantizeJob& j = jobs[i];
+      const int64_t words = j.rows * j.cols * bits / 32;
+      if (words == 0) continue;
+      b.start[b.n] = v;
+      b.words[b.n] = words;
+      b.codes[b.n] = static_cast<const uint32_t*>(j.codes);
+      b.scales[b.n] = static_cast<const uint16_t*>(j.scales);
+      b.biases[b.n] = static_cast<const uint16_t*>(j.biases);
+      b.out[b.n] = static_cast<uint16_t*>(j.w);
+      v += (words + kSpan - 1) / kSpan * kSpan;  // whole warp spans
+      ++b.n;
+    }
+    if (b.n == 0) break;
+    b.start[b.n] = v;
+    const int grid = grid_for(v / kWords, 256);
+    if (bits == 4)
+      dequantize_batch_kernel<4><<<grid, 256, 0, s>>>(b, shift);
+    else
+      dequantize_batch_kernel<8><<<grid, 256, 0, s>>>(b, shift);
+    rc = check_cuda(cudaGetLastError(), "dequantize_batch launch");
+    if (rc) return rc;
+  }
+  return TQ_OK;
 }

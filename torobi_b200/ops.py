@@ -14,7 +14,7 @@ from __future__ import annotations
 
 import torch
 
-from ._lib import TQ_DTYPE_BF16, TQ_DTYPE_F32, check, lib
+from ._lib import TQ_DTYPE_BF16, TQ_DTYPE_F32, TqDequantizeJob, TqQuantizeJob, check, lib
 
 SUPPORTED_BITS = (4, 8)
 SUPPORTED_GROUPS = (32, 64, 128)
@@ -163,6 +163,72 @@ def dequantize(w_q: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
             _ptr(w_q.contiguous()), _ptr(scales.contiguous()), _ptr(biases.contiguous()), rows,
             cols, group_size, bits, _ptr(out), _stream()))
     return out
+
+
+def quantize_batch(ws, group_size: int = 64, bits: int = 4):
+    """``quantize`` of every matrix in ``ws`` in one launch (one per 256
+    matrices): a list of ``(w_q, scales, biases)`` in the same order."""
+    op = "quantize_batch"
+    ws = list(ws)
+    _check_bits_group(op, group_size, bits)
+    outs, keep = [], []
+    jobs = (TqQuantizeJob * max(len(ws), 1))()
+    for i, w in enumerate(ws):
+        _need_cuda(op, w=w)
+        if w.dim() < 2 or w.dtype != torch.bfloat16:
+            raise ValueError(f"[{op}] matrix {i}: bfloat16 with at least 2 dimensions needed, "
+                             f"got {w.dtype} {tuple(w.shape)}")
+        cols = w.shape[-1]
+        if cols % group_size != 0:
+            raise ValueError(f"[{op}] matrix {i}: the last dimension ({cols}) must be divisible "
+                             f"by the group size {group_size}")
+        if w.device != ws[0].device:
+            raise ValueError(f"[{op}] every matrix must be on {ws[0].device}")
+        w2 = w.contiguous().reshape(-1, cols)
+        lead = tuple(w.shape[:-1])
+        codes = torch.empty(lead + (cols * bits // 32,), dtype=torch.uint32, device=w.device)
+        scales = torch.empty(lead + (cols // group_size,), dtype=torch.bfloat16, device=w.device)
+        biases = torch.empty_like(scales)
+        jobs[i] = TqQuantizeJob(_ptr(w2), w2.shape[0], cols, _ptr(codes), _ptr(scales),
+                                _ptr(biases))
+        keep.append(w2)
+        outs.append((codes, scales, biases))
+    if ws:
+        with torch.cuda.device(ws[0].device):
+            _launch("quantize", lambda: lib().tq_quantize_batch(jobs, len(ws), group_size, bits,
+                                                                _stream()))
+    del keep  # temporaries go back to the caching allocator, reused only in stream order
+    return outs
+
+
+def dequantize_batch(packed, group_size: int = 64, bits: int = 4):
+    """``dequantize`` of every ``(w_q, scales, biases)`` in ``packed`` in one
+    launch (one per 256): a list of bf16 matrices in the same order."""
+    op = "dequantize_batch"
+    packed = list(packed)
+    _check_bits_group(op, group_size, bits)
+    outs, keep = [], []
+    jobs = (TqDequantizeJob * max(len(packed), 1))()
+    for i, (w_q, scales, biases) in enumerate(packed):
+        _need_cuda(op, w_q=w_q, scales=scales, biases=biases)
+        if w_q.dim() < 2:
+            raise ValueError(f"[{op}] matrix {i}: the packed matrix needs at least 2 dimensions")
+        cols = _check_packed(op, w_q, scales, biases, group_size, bits)
+        lead = tuple(w_q.shape[:-1])
+        rows = 1
+        for d in lead:
+            rows *= d
+        c, s_, b_ = w_q.contiguous(), scales.contiguous(), biases.contiguous()
+        out = torch.empty(lead + (cols,), dtype=torch.bfloat16, device=w_q.device)
+        jobs[i] = TqDequantizeJob(_ptr(c), _ptr(s_), _ptr(b_), rows, cols, _ptr(out))
+        keep += [c, s_, b_]
+        outs.append(out)
+    if packed:
+        with torch.cuda.device(packed[0][0].device):
+            _launch("dequantize", lambda: lib().tq_dequantize_batch(jobs, len(packed), group_size,
+                                                                    bits, _stream()))
+    del keep
+    return outs
 
 
 def lora_merge(w_q: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
