@@ -277,7 +277,17 @@ int tq_rmsnorm_fwd(const void* x, const void* w, int64_t rows, int64_t hidden, f
                    float* rstd, void* stream);
 
 /*
- * Its input gradient (the gain is frozen in QLoRA, so no dw):
+ * The pre-norm block's residual add and the norm after it in one pass:
+ *   s = RNE_bf16(x + res)  (the residual stream, written to s)
+ *   y = RMSNorm(s) * w     (of the stored s; rstd as above)
+ * Replaces Op::Add (engine/src/interp.rs:198) followed by the RMSNorm
+ * above; its backward is tq_rmsnorm_bwd on s with dres = the gradient of s.
+ */
+int tq_add_rmsnorm_fwd(const void* x, const void* res, const void* w, int64_t rows,
+                       int64_t hidden, float eps, void* s, void* y, float* rstd, void* stream);
+
+/*
+ * The RMSNorm's input gradient (the gain is frozen in QLoRA, so no dw):
  *   dx = rstd * dy * w - x * rstd^3 * mean(dy * w * x)  (+ dres, if not NULL).
  */
 int tq_rmsnorm_bwd(const void* x, const void* w, const float* rstd, const void* dy,

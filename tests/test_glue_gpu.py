@@ -33,6 +33,39 @@ def test_rms_norm(cuda, rows, hidden):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("rows,hidden", [(1, 8), (37, 896), (4096, 4096), (3, 14336)])
+def test_add_rms_norm(cuda, rows, hidden):
+    """s = x + res and its norm in one kernel: s and y bit-equal to the
+    separate bf16 add and rms_norm; the gradients of x and res (the norm's
+    backward with the stream's gradient added inside) against f32, and the
+    stream's gradient alone passed through when the norm output is unused."""
+    import torch
+
+    from torobi_b200 import glue
+
+    torch.manual_seed(rows + 1)
+    x = (torch.randn(rows, hidden, device=cuda) * 3).bfloat16().requires_grad_()
+    res = torch.randn(rows, hidden, device=cuda).bfloat16().requires_grad_()
+    w = (torch.rand(hidden, device=cuda) + 0.5).bfloat16()
+    ds = torch.randn(rows, hidden, device=cuda).bfloat16()
+    dy = torch.randn(rows, hidden, device=cuda).bfloat16()
+    s, y = glue.add_rms_norm(x, res, w, 1e-6)
+    s_sep = x.detach() + res.detach()
+    assert torch.equal(s.detach().view(torch.int16), s_sep.view(torch.int16))
+    y_sep = glue.rms_norm(s_sep, w, 1e-6)
+    assert torch.equal(y.detach().view(torch.int16), y_sep.view(torch.int16))
+    dx, dres = torch.autograd.grad((s, y), (x, res), (ds, dy))
+    sf = s_sep.float().requires_grad_()
+    ref = sf * torch.rsqrt(sf.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()
+    (dref,) = torch.autograd.grad(ref, sf, dy.float())
+    dref = dref + ds.float()
+    assert _rel(dx, dref) < TOL and torch.equal(dx, dres)
+    s2, _ = glue.add_rms_norm(x, res, w, 1e-6)
+    (dx2,) = torch.autograd.grad(s2, x, ds)
+    assert torch.equal(dx2, ds)
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("b,s,h,d", [(2, 16, 4, 64), (1, 2048, 8, 128), (3, 7, 14, 64)])
 def test_rope_and_its_inverse(cuda, b, s, h, d):
     import torch

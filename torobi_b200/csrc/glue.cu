@@ -40,19 +40,44 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 // One warp per row; H % 8 == 0.
+// ADD: the row is s = RNE_bf16(x + res), written to s_out, and the norm is
+// taken of that stored s (the residual add and the norm that follows it in
+// the pre-norm block, in one pass; the second pass recomputes s from x and
+// res rather than reading back its own stores).
+template <bool ADD>
 __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const uint4* __restrict__ x,
+                                                          const uint4* __restrict__ res,
                                                           const uint4* __restrict__ w, int64_t rows,
                                                           int hv, float eps,
+                                                          uint4* __restrict__ s_out,
                                                           uint4* __restrict__ y,
                                                           float* __restrict__ rstd) {
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
   const uint4* xr = x + row * hv;
+  const uint4* rr = ADD ? res + row * hv : nullptr;
+  auto load_row = [&](int i, float (&f)[8]) {
+    if constexpr (ADD) {
+      float e[8];
+      bf8_to_f32(__ldg(xr + i), f);
+      bf8_to_f32(__ldg(rr + i), e);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] += e[j];
+      const uint4 sv = f32_to_bf8(f);  // the stored residual stream
+      bf8_to_f32(sv, f);
+      return sv;
+    } else {
+      const uint4 sv = __ldg(xr + i);
+      bf8_to_f32(sv, f);
+      return sv;
+    }
+  };
   float ss = 0.0f;
   for (int i = lane; i < hv; i += 32) {
     float f[8];
-    bf8_to_f32(__ldg(xr + i), f);
+    const uint4 sv = load_row(i, f);
+    if constexpr (ADD) s_out[row * hv + i] = sv;
 #pragma unroll
     for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
   }
@@ -62,7 +87,7 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const uint4* __restric
   uint4* yr = y + row * hv;
   for (int i = lane; i < hv; i += 32) {
     float f[8], g[8];
-    bf8_to_f32(__ldg(xr + i), f);
+    load_row(i, f);
     bf8_to_f32(__ldg(w + i), g);
 #pragma unroll
     for (int j = 0; j < 8; ++j) f[j] = f[j] * r * g[j];
@@ -216,10 +241,30 @@ extern "C" int tq_rmsnorm_fwd(const void* x, const void* w, int64_t rows, int64_
     return fail(TQ_ERR_MISALIGNED, "rmsnorm: x, w and y must be 16-byte aligned");
   const int warps = 8;
   const unsigned grid = static_cast<unsigned>((rows + warps - 1) / warps);
-  rmsnorm_fwd_kernel<<<grid, warps * 32, 0, as_stream(stream)>>>(
-      static_cast<const uint4*>(x), static_cast<const uint4*>(w), rows,
-      static_cast<int>(hidden / 8), eps, static_cast<uint4*>(y), rstd);
+  rmsnorm_fwd_kernel<false><<<grid, warps * 32, 0, as_stream(stream)>>>(
+      static_cast<const uint4*>(x), nullptr, static_cast<const uint4*>(w), rows,
+      static_cast<int>(hidden / 8), eps, nullptr, static_cast<uint4*>(y), rstd);
   return check_cuda(cudaGetLastError(), "rmsnorm_fwd launch");
+}
+
+extern "C" int tq_add_rmsnorm_fwd(const void* x, const void* res, const void* w, int64_t rows,
+                                  int64_t hidden, float eps, void* s, void* y, float* rstd,
+                                  void* stream) {
+  using namespace tq;
+  if (rows < 0 || hidden <= 0 || hidden % 8 != 0)
+    return fail(TQ_ERR_INVALID, "add_rmsnorm: hidden (%lld) must be a positive multiple of 8",
+                (long long)hidden);
+  if (rows == 0) return TQ_OK;
+  if (!x || !res || !w || !s || !y) return fail(TQ_ERR_INVALID, "add_rmsnorm: null pointer");
+  if (!a16(x) || !a16(res) || !a16(w) || !a16(s) || !a16(y) || (rstd && !aligned(rstd, 4)))
+    return fail(TQ_ERR_MISALIGNED, "add_rmsnorm: x, res, w, s and y must be 16-byte aligned");
+  const int warps = 8;
+  const unsigned grid = static_cast<unsigned>((rows + warps - 1) / warps);
+  rmsnorm_fwd_kernel<true><<<grid, warps * 32, 0, as_stream(stream)>>>(
+      static_cast<const uint4*>(x), static_cast<const uint4*>(res), static_cast<const uint4*>(w),
+      rows, static_cast<int>(hidden / 8), eps, static_cast<uint4*>(s), static_cast<uint4*>(y),
+      rstd);
+  return check_cuda(cudaGetLastError(), "add_rmsnorm_fwd launch");
 }
 
 extern "C" int tq_rmsnorm_bwd(const void* x, const void* w, const float* rstd, const void* dy,

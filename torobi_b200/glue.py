@@ -52,6 +52,51 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     return _RMSNorm.apply(x, w, eps)
 
 
+class _AddRMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, res, w, eps):
+        _need_cuda("add_rms_norm", x=x, res=res, w=w)
+        x = _bf16_contig("x", x)
+        res = _bf16_contig("res", res)
+        w = _bf16_contig("w", w)
+        if res.shape != x.shape:
+            raise ValueError(f"[add_rms_norm] res {tuple(res.shape)} must match x "
+                             f"{tuple(x.shape)}")
+        h = x.shape[-1]
+        rows = x.numel() // h
+        s = torch.empty_like(x)
+        y = torch.empty_like(x)
+        rstd = torch.empty(rows, dtype=torch.float32, device=x.device)
+        _launch("rmsnorm", lambda: lib().tq_add_rmsnorm_fwd(
+            _ptr(x), _ptr(res), _ptr(w), rows, h, float(eps), _ptr(s), _ptr(y), _ptr(rstd),
+            _stream()))
+        ctx.save_for_backward(s, w, rstd)
+        ctx.set_materialize_grads(False)
+        return s, y
+
+    @staticmethod
+    def backward(ctx, ds, dy):
+        s, w, rstd = ctx.saved_tensors
+        if dy is None:
+            return ds, ds, None, None
+        dy = dy.contiguous()
+        ds = ds.contiguous() if ds is not None else None
+        h = s.shape[-1]
+        rows = s.numel() // h
+        dx = torch.empty_like(s)
+        _launch("rmsnorm", lambda: lib().tq_rmsnorm_bwd(
+            _ptr(s), _ptr(w), _ptr(rstd), _ptr(dy), _ptr(ds) if ds is not None else None, rows, h,
+            _ptr(dx), _stream()))
+        return dx, dx, None, None
+
+
+def add_rms_norm(x: torch.Tensor, res: torch.Tensor, w: torch.Tensor, eps: float):
+    """``(s, rms_norm(s, w, eps))`` with ``s = x + res`` in bf16: a pre-norm
+    block's residual add and the norm after it in one kernel; its backward
+    adds the residual stream's gradient inside the norm's (one kernel)."""
+    return _AddRMSNorm.apply(x, res, w, eps)
+
+
 class _RoPE(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, cos, sin, seq):

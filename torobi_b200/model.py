@@ -13,7 +13,8 @@ over next-token targets.
 
 Every linear of every block is a ``QuantizedWeight`` (MLX affine codes) run by
 the tcgen05 quantized GEMM; adapted linears add the fused LoRA branch.  The
-norms, RoPE and SwiGLU between them are fused kernels (``glue``); attention
+norms (each residual add fused into the norm after it), RoPE and SwiGLU
+between them are fused kernels (``glue``); attention
 (PyTorch SDPA), the bf16 head and the loss are library calls -- they are
 outside the quantized-weight path this package replaces.
 The head stays bf16 (a plain library GEMM): QLoRA quantizes the blocks'
@@ -220,11 +221,15 @@ class QLoRACausalLM:
             self._rope_cache[seq] = t
         return t
 
-    def block_forward(self, blk: Block, x: torch.Tensor) -> torch.Tensor:
+    def block_forward(self, blk: Block, x: torch.Tensor, h: torch.Tensor,
+                      next_norm: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """One pre-norm block on the residual stream ``x`` whose input norm
+        ``h`` is already computed; returns the new stream and its norm under
+        ``next_norm`` (the next block's input norm, or the final norm).  Each
+        residual add is fused with the norm that follows it."""
         cfg = self.cfg
         B, S, H = x.shape
         cos, sin = self._rope(S)
-        h = glue.rms_norm(x, blk.input_norm, cfg.rms_eps)
         q = qlora_linear(h, blk.linears["q_proj"], blk.adapters["q_proj"])
         k = qlora_linear(h, blk.linears["k_proj"], blk.adapters["k_proj"])
         v = qlora_linear(h, blk.linears["v_proj"], blk.adapters["v_proj"])
@@ -236,18 +241,26 @@ class QLoRACausalLM:
                                              v.transpose(1, 2), is_causal=True,
                                              enable_gqa=cfg.heads != cfg.kv_heads)
         att = att.transpose(1, 2).reshape(B, S, cfg.heads * cfg.head_dim)
-        x = x + qlora_linear(att, blk.linears["o_proj"], blk.adapters["o_proj"])
-        h = glue.rms_norm(x, blk.post_norm, cfg.rms_eps)
+        x, h = glue.add_rms_norm(x, qlora_linear(att, blk.linears["o_proj"],
+                                                 blk.adapters["o_proj"]),
+                                 blk.post_norm, cfg.rms_eps)
         g = qlora_linear(h, blk.linears["gate_proj"], blk.adapters["gate_proj"])
         u = qlora_linear(h, blk.linears["up_proj"], blk.adapters["up_proj"])
-        return x + qlora_linear(glue.swiglu(g, u), blk.linears["down_proj"],
-                                blk.adapters["down_proj"])
+        return glue.add_rms_norm(x, qlora_linear(glue.swiglu(g, u), blk.linears["down_proj"],
+                                                 blk.adapters["down_proj"]),
+                                 next_norm, cfg.rms_eps)
 
     def hidden(self, ids: torch.Tensor) -> torch.Tensor:
+        """The final-normed hidden states: the blocks' residual stream
+        (``x += attn(norm(x)); x += mlp(norm(x))``) and the final norm."""
         x = F.embedding(ids, self.embed)
-        for blk in self.blocks:
-            x = self.block_forward(blk, x)
-        return glue.rms_norm(x, self.final_norm, self.cfg.rms_eps)
+        if not self.blocks:
+            return glue.rms_norm(x, self.final_norm, self.cfg.rms_eps)
+        h = glue.rms_norm(x, self.blocks[0].input_norm, self.cfg.rms_eps)
+        for i, blk in enumerate(self.blocks):
+            nxt = self.blocks[i + 1].input_norm if i + 1 < len(self.blocks) else self.final_norm
+            x, h = self.block_forward(blk, x, h, nxt)
+        return h
 
     def logits(self, h: torch.Tensor) -> torch.Tensor:
         head = self.embed if self.lm_head is None else self.lm_head
