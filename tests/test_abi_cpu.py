@@ -48,6 +48,32 @@ def test_host_side_argument_errors_need_no_gpu():
     assert rc == TQ_ERR_INVALID and b"step count" in L.tq_last_error()
     rc = L.tq_lora_grad(dummy, dummy, 4, 8, 12, 8, 0, 0, dummy, None)
     assert rc == TQ_ERR_INVALID and b"multiple of 8" in L.tq_last_error()
+    rc = L.tq_add_rmsnorm_fwd(dummy, dummy, dummy, 4, 12, 1e-6, dummy, dummy, None, None)
+    assert rc == TQ_ERR_INVALID and b"multiple of 8" in L.tq_last_error()
+    rc = L.tq_wait_selftest(10, None)
+    assert rc == TQ_ERR_INVALID and b"limit_ns" in L.tq_last_error()
+
+
+def test_batch_entry_points_check_every_job_first():
+    import torobi_b200 as tq
+    from torobi_b200._lib import (TQ_ERR_INVALID, TQ_ERR_MISALIGNED, TQ_ERR_UNSUPPORTED,
+                                  TqDequantizeJob, TqQuantizeJob)
+
+    L = tq.lib()
+    p = 4096  # a 16-byte aligned stand-in address; nothing is dereferenced
+    good = TqQuantizeJob(p, 4, 64, p, p, p)
+    jobs = (TqQuantizeJob * 3)(good, TqQuantizeJob(p, 0, 64, 0, 0, 0), TqQuantizeJob(p, 4, 96, p, p, p))
+    assert L.tq_quantize_batch(jobs, 3, 64, 4, None) == TQ_ERR_INVALID
+    assert b"job 2" in L.tq_last_error() and b"divisible" in L.tq_last_error()
+    jobs[2] = TqQuantizeJob(p + 8, 4, 64, p, p, p)
+    assert L.tq_quantize_batch(jobs, 3, 64, 4, None) == TQ_ERR_MISALIGNED
+    assert b"job 2" in L.tq_last_error()
+    assert L.tq_quantize_batch(jobs, 3, 48, 4, None) == TQ_ERR_UNSUPPORTED
+    assert L.tq_quantize_batch(None, 2, 64, 4, None) == TQ_ERR_INVALID
+    djobs = (TqDequantizeJob * 1)(TqDequantizeJob(p, p, p, 4, 64, 0))
+    assert L.tq_dequantize_batch(djobs, 1, 64, 4, None) == TQ_ERR_INVALID
+    assert b"job 0" in L.tq_last_error() and b"null" in L.tq_last_error()
+    assert L.tq_dequantize_batch(djobs, 1, 64, 5, None) == TQ_ERR_UNSUPPORTED
 
 
 def test_ops_refuse_cpu_tensors():
@@ -57,3 +83,9 @@ def test_ops_refuse_cpu_tensors():
     w = torch.zeros((8, 64), dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="CUDA"):
         tq.quantize(w, 64, 4)
+    with pytest.raises(ValueError, match="CUDA"):
+        tq.quantize_batch([w], 64, 4)
+    from torobi_b200 import glue
+
+    with pytest.raises(ValueError, match="CUDA"):
+        glue.add_rms_norm(w, w, w[0], 1e-6)
