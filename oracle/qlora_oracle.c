@@ -28,8 +28,10 @@
  *   codes packed low-bits-first, 32/bits codes per uint32 along the last axis;
  *   scale and bias stored in the weight's dtype (bf16, round-to-nearest-even).
  *
- * Conventions this file fixes (MLX itself cannot be run here, so bit-exactness
- * against MLX is unpinned; the kernels are held bit-exact to THIS file):
+ * Parity unpinned for quantize / dequantize / quantized_matmul: MLX itself
+ * cannot be run here and the reference holds no golden vectors for these
+ * ops, so bit-exactness against MLX is unverified.  The conventions this file
+ * fixes (the kernels are held bit-exact to THIS file):
  *   - all group arithmetic in IEEE f32 with round-to-nearest-even, no FMA
  *     contraction (compiled with -ffp-contract=off);
  *   - max/min follow C++ std::max/std::min (`a < b ? b : a`), so a NaN element
