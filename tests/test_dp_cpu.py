@@ -88,3 +88,88 @@ def test_two_gloo_ranks_match_one_process():
     for t in range(1, 4):
         w, m, v = O.adamw_step(w, _grads(w, xs, ys), m, v, t, lr=0.1)
     np.testing.assert_allclose(w0, w, rtol=1e-5, atol=1e-6)
+
+
+def _gate_worker(rank, world, init, out_dir, fail_rank, timeout):
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
+    from torobi_b200.train import RankLost, StepGate
+
+    dist.init_process_group("gloo", init_method=init, rank=rank, world_size=world)
+    gate = StepGate(dist.distributed_c10d._get_default_store(), rank, world, timeout=timeout)
+    result = "ok"
+    t0 = time.monotonic()
+    try:
+        for step in range(3):
+            if rank == fail_rank and step == 1:
+                raise RuntimeError("injected failure before step 1's collective")
+            gate.wait(step)
+            t = torch.ones(1)
+            dist.all_reduce(t)
+            assert t.item() == world
+    except RankLost:
+        result = f"lost {time.monotonic() - t0:.2f}"
+    except RuntimeError:
+        result = "raised"
+    (Path(out_dir) / f"r{rank}.txt").write_text(result)
+    os._exit(0)  # no teardown handshake with a rank that is gone
+
+
+def _free_port():
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("store", ["file", "tcp"])
+@pytest.mark.parametrize("fail_rank", [-1, 1])
+def test_step_gate_reports_a_lost_rank_before_the_collective(store, fail_rank):
+    """Three steps on two gloo ranks, each step's collective behind the gate.
+    With every rank alive all steps run; when rank 1 raises before step 1,
+    rank 0 learns it on the host (RankLost after the gate's 2 s) instead of
+    waiting in the collective."""
+    import torch.multiprocessing as mp
+
+    with tempfile.TemporaryDirectory() as d:
+        init = f"file://{os.path.join(d, 'init')}" if store == "file" else \
+            f"tcp://127.0.0.1:{_free_port()}"
+        ctx = mp.get_context("spawn")
+        procs = [ctx.Process(target=_gate_worker, args=(r, 2, init, d, fail_rank, 2.0))
+                 for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(90)
+            if p.exitcode is None:
+                p.kill()
+            assert p.exitcode == 0
+        r0 = (Path(d) / "r0.txt").read_text()
+        r1 = (Path(d) / "r1.txt").read_text()
+    if fail_rank < 0:
+        assert (r0, r1) == ("ok", "ok")
+    else:
+        assert r1 == "raised"
+        assert r0.startswith("lost"), r0
+        assert float(r0.split()[1]) < 30.0
+
+
+def test_step_gate_alone():
+    import torch.distributed as dist
+
+    from torobi_b200.train import RankLost, StepGate
+
+    store = dist.HashStore()
+    StepGate(store, 0, 1, timeout=0.1).wait(0)  # one rank: nothing to wait for
+    gate = StepGate(store, 0, 2, timeout=0.2)
+    with pytest.raises(RankLost, match="1 of 2 ranks did not reach step 5"):
+        gate.wait(5)
+    store.add("torobi_b200/step/6", 1)  # the other rank got there first
+    gate.wait(6)
+    with pytest.raises(ValueError):
+        StepGate(store, 0, 2, timeout=0)

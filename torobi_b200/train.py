@@ -19,6 +19,7 @@ from __future__ import annotations
 import ctypes
 import math
 import os
+import time
 from dataclasses import dataclass
 
 import torch
@@ -91,6 +92,49 @@ class NcclGradReduce:
             self.comm = None
 
 
+class RankLost(RuntimeError):
+    """A rank did not reach a step's collective in time (it raised, exited or
+    stalled); raised on the host before any collective of that step is
+    launched, so no rank is left waiting inside NCCL."""
+
+
+class StepGate:
+    """Host-side liveness check before each step's collectives.
+
+    Every rank checks in under the step's key of the torch.distributed store
+    (one ``add``) and waits, polling, until all ``world`` ranks have; a rank
+    that has not arrived within ``timeout`` seconds is reported as lost with
+    ``RankLost``.  An NCCL allreduce whose peer has died never returns, so the
+    check is made before the allreduce is launched: the surviving ranks leave
+    the step between kernels, with nothing of theirs in flight.  The reference
+    has one process and nothing like this (its runtime poisons itself on a
+    panic, engine/src/runtime.rs:105-117); it is the data-parallel form of
+    "a failed step does not hang the next one".
+    """
+
+    def __init__(self, store, rank: int, world: int, timeout: float = 240.0,
+                 prefix: str = "torobi_b200/step"):
+        if timeout <= 0:
+            raise ValueError(f"timeout must be positive, got {timeout}")
+        self.store, self.rank, self.world = store, rank, world
+        self.timeout, self.prefix = float(timeout), prefix
+
+    def wait(self, step: int) -> None:
+        if self.world == 1:
+            return
+        key = f"{self.prefix}/{step}"
+        arrived = self.store.add(key, 1)
+        deadline = time.monotonic() + self.timeout
+        pause = 0.0005
+        while arrived < self.world:
+            if time.monotonic() > deadline:
+                raise RankLost(f"rank {self.rank}: {self.world - arrived} of {self.world} ranks "
+                               f"did not reach step {step} within {self.timeout:g} s")
+            time.sleep(pause)
+            pause = min(pause * 2, 0.05)
+            arrived = self.store.add(key, 0)
+
+
 @dataclass
 class AdamWConfig:
     lr: float = 1e-4
@@ -106,8 +150,11 @@ class Trainer:
 
     def __init__(self, model, opt: AdamWConfig | None = None, micro_batch: int = 1,
                  reduce: NcclGradReduce | None = None, rank: int = 0, world: int = 1,
-                 graph: bool = False):
+                 graph: bool = False, gate: StepGate | None = None):
         self.model = model
+        # gate (several ranks): checked on the host before each step's
+        # allreduce, so a lost rank raises RankLost instead of hanging NCCL.
+        self.gate = gate
         # graph=True replays the forward and backward of every micro-batch as
         # one CUDA graph (captured on the first step of a batch shape); the
         # collective and the optimizer stay outside it (AdamW takes the step
@@ -168,6 +215,8 @@ class Trainer:
             g.replay()
         else:
             self._gradients(ids)
+        if self.gate is not None:
+            self.gate.wait(self.steps)
         self.reduce(st.grads)
         self.reduce(self.loss_buf)
         self.loss_buf /= float(self.world * len(parts))
