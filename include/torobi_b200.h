@@ -364,6 +364,13 @@ int tq_dp_unique_id(void* id128);
 int tq_dp_comm_init(void** comm, const void* id128, int nranks, int rank);
 int tq_dp_allreduce_sum(void* comm, void* buf, int64_t count, int dtype, void* stream);
 int tq_dp_comm_destroy(void* comm);
+/*
+ * Ends a communicator without waiting for its peers, for use after a rank
+ * has been lost (its collectives may never complete, so a destroy could
+ * wait for good).  The reference has no counterpart (one process, no
+ * collective); NULL is a no-op.
+ */
+int tq_dp_comm_abort(void* comm);
 
 #ifdef __cplusplus
 }

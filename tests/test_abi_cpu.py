@@ -52,6 +52,7 @@ def test_host_side_argument_errors_need_no_gpu():
     assert rc == TQ_ERR_INVALID and b"multiple of 8" in L.tq_last_error()
     rc = L.tq_wait_selftest(10, None)
     assert rc == TQ_ERR_INVALID and b"limit_ns" in L.tq_last_error()
+    assert L.tq_dp_comm_abort(None) == 0 and L.tq_dp_comm_destroy(None) == 0
 
 
 def test_batch_entry_points_check_every_job_first():

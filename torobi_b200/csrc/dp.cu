@@ -56,3 +56,10 @@ extern "C" int tq_dp_comm_destroy(void* comm) {
   if (!comm) return TQ_OK;
   return check_nccl(ncclCommDestroy(static_cast<ncclComm_t>(comm)), "ncclCommDestroy");
 }
+
+// After a lost rank: frees the communicator without waiting for its peers
+// (ncclCommDestroy may wait on operations a dead peer never completes).
+extern "C" int tq_dp_comm_abort(void* comm) {
+  if (!comm) return TQ_OK;
+  return check_nccl(ncclCommAbort(static_cast<ncclComm_t>(comm)), "ncclCommAbort");
+}

@@ -91,6 +91,12 @@ class NcclGradReduce:
             check(lib().tq_dp_comm_destroy(self.comm))
             self.comm = None
 
+    def abort(self) -> None:
+        """Frees the communicator without its peers, after ``RankLost``."""
+        if self.comm is not None:
+            check(lib().tq_dp_comm_abort(self.comm))
+            self.comm = None
+
 
 class RankLost(RuntimeError):
     """A rank did not reach a step's collective in time (it raised, exited or
@@ -216,7 +222,13 @@ class Trainer:
         else:
             self._gradients(ids)
         if self.gate is not None:
-            self.gate.wait(self.steps)
+            try:
+                self.gate.wait(self.steps)
+            except RankLost:
+                abort = getattr(self.reduce, "abort", None)
+                if abort is not None:
+                    abort()  # the communicator's peers are gone: do not wait on them
+                raise
         self.reduce(st.grads)
         self.reduce(self.loss_buf)
         self.loss_buf /= float(self.world * len(parts))
