@@ -143,22 +143,25 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const uint4* __restric
 // x [tokens, heads, dim] bf16 with tokens = batch * seq (position = token %
 // seq); cos/sin [seq, dim/2] f32.  One thread per 8 pairs.  sign = -1 applies
 // the inverse rotation (the backward).
+// I: the index type, 32-bit whenever the launch's items fit (the per-item
+// divisions by heads and seq are then 32-bit; 64-bit ones cost several
+// times more and bounded this kernel).
+template <typename I>
 __global__ void __launch_bounds__(256) rope_kernel(const uint4* __restrict__ x, int64_t tokens,
                                                    int heads, int dim, int seq,
                                                    const float* __restrict__ cosv,
                                                    const float* __restrict__ sinv, float sign,
                                                    uint4* __restrict__ y) {
   const int half = dim / 2;
-  const int per_head = half / 8;  // threads per head
-  const int64_t n = tokens * heads * per_head;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < n;
-       idx += stride) {
+  const I per_head = static_cast<I>(half / 8);  // threads per head
+  const I n = static_cast<I>(tokens) * static_cast<I>(heads) * per_head;
+  const I stride = static_cast<I>(gridDim.x) * blockDim.x;
+  for (I idx = static_cast<I>(blockIdx.x) * blockDim.x + threadIdx.x; idx < n; idx += stride) {
     const int c = static_cast<int>(idx % per_head);
-    const int64_t th = idx / per_head;            // token * heads + head
-    const int64_t token = th / heads;
-    const int pos = static_cast<int>(token % seq);
-    const int64_t base = th * (dim / 8);          // in 16-byte vectors
+    const I th = idx / per_head;                  // token * heads + head
+    const I token = th / static_cast<I>(heads);
+    const int pos = static_cast<int>(token % static_cast<I>(seq));
+    const int64_t base = static_cast<int64_t>(th) * (dim / 8);  // in 16-byte vectors
     float a[8], b[8];
     bf8_to_f32(__ldg(x + base + c), a);
     bf8_to_f32(__ldg(x + base + per_head + c), b);
@@ -301,9 +304,16 @@ extern "C" int tq_rope(const void* x, int64_t tokens, int64_t heads, int64_t dim
   if (!a16(x) || !a16(y) || !a16(cosv) || !a16(sinv))
     return fail(TQ_ERR_MISALIGNED, "rope: tensors must be 16-byte aligned");
   const int64_t n = tokens * heads * (dim / 16);
-  rope_kernel<<<grid_for(n, 256), 256, 0, as_stream(stream)>>>(
-      static_cast<const uint4*>(x), tokens, static_cast<int>(heads), static_cast<int>(dim),
-      static_cast<int>(seq), cosv, sinv, inverse ? -1.0f : 1.0f, static_cast<uint4*>(y));
+  const int grid = grid_for(n, 256);
+  // 32-bit indices while every index the grid-stride loop forms fits.
+  if (n + static_cast<int64_t>(grid) * 256 < (1ll << 32))
+    rope_kernel<uint32_t><<<grid, 256, 0, as_stream(stream)>>>(
+        static_cast<const uint4*>(x), tokens, static_cast<int>(heads), static_cast<int>(dim),
+        static_cast<int>(seq), cosv, sinv, inverse ? -1.0f : 1.0f, static_cast<uint4*>(y));
+  else
+    rope_kernel<int64_t><<<grid, 256, 0, as_stream(stream)>>>(
+        static_cast<const uint4*>(x), tokens, static_cast<int>(heads), static_cast<int>(dim),
+        static_cast<int>(seq), cosv, sinv, inverse ? -1.0f : 1.0f, static_cast<uint4*>(y));
   return check_cuda(cudaGetLastError(), "rope launch");
 }
 
