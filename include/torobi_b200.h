@@ -282,6 +282,8 @@ int tq_rmsnorm_fwd(const void* x, const void* w, int64_t rows, int64_t hidden, f
  *   y = RMSNorm(s) * w     (of the stored s; rstd as above)
  * Replaces Op::Add (engine/src/interp.rs:198) followed by the RMSNorm
  * above; its backward is tq_rmsnorm_bwd on s with dres = the gradient of s.
+ * There is no in-place form: s and y must not overlap x, res or each other
+ * (refused with TQ_ERR_INVALID).
  */
 int tq_add_rmsnorm_fwd(const void* x, const void* res, const void* w, int64_t rows,
                        int64_t hidden, float eps, void* s, void* y, float* rstd, void* stream);
@@ -371,6 +373,15 @@ int tq_dp_comm_destroy(void* comm);
  * collective); NULL is a no-op.
  */
 int tq_dp_comm_abort(void* comm);
+/*
+ * The communicator's asynchronous error (ncclCommGetAsyncError) in
+ * *nccl_result: 0 while healthy, an ncclResult_t code once a collective has
+ * failed (e.g. a peer's connection closed).  A host that waits for a
+ * collective under a deadline polls it beside the collective's completion
+ * and aborts the communicator on an error or when the deadline passes.  No
+ * reference counterpart (one process, no collective).
+ */
+int tq_dp_comm_async_error(void* comm, int* nccl_result);
 
 #ifdef __cplusplus
 }

@@ -83,9 +83,10 @@ def num_threads() -> int:
 def bf16_from_f32(x) -> np.ndarray:
     """f32 -> bf16 bit patterns, round to nearest even (NaN -> 0x7FC0)."""
     x = np.ascontiguousarray(x, dtype=np.float32)
-    u = x.view(np.uint32).astype(np.uint64)
-    lsb = (u >> 16) & 1
-    r = ((u + 0x7FFF + lsb) >> 16).astype(np.uint16)
+    u = x.view(np.uint32)
+    # u + 0x7FFF + lsb wraps in 32 bits only for NaN patterns, replaced below.
+    r = ((u + (np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1)))) >> np.uint32(16))
+    r = r.astype(np.uint16)
     r[np.isnan(x)] = 0x7FC0
     return r
 

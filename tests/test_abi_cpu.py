@@ -50,6 +50,12 @@ def test_host_side_argument_errors_need_no_gpu():
     assert rc == TQ_ERR_INVALID and b"multiple of 8" in L.tq_last_error()
     rc = L.tq_add_rmsnorm_fwd(dummy, dummy, dummy, 4, 12, 1e-6, dummy, dummy, None, None)
     assert rc == TQ_ERR_INVALID and b"multiple of 8" in L.tq_last_error()
+    p = 1 << 20  # 16-byte aligned stand-in addresses; nothing is dereferenced
+    rows, hid = 4, 64
+    for s_ptr, y_ptr in ((p, p + 4096), (p + (1 << 16), p + 64)):  # s over x; y over x
+        rc = L.tq_add_rmsnorm_fwd(p, p + (1 << 14), p + (1 << 15), rows, hid, 1e-6, s_ptr,
+                                  y_ptr, None, None)
+        assert rc == TQ_ERR_INVALID and b"overlap" in L.tq_last_error()
     rc = L.tq_wait_selftest(10, None)
     assert rc == TQ_ERR_INVALID and b"limit_ns" in L.tq_last_error()
     assert L.tq_dp_comm_abort(None) == 0 and L.tq_dp_comm_destroy(None) == 0

@@ -169,7 +169,118 @@ def test_step_gate_alone():
     gate = StepGate(store, 0, 2, timeout=0.2)
     with pytest.raises(RankLost, match="1 of 2 ranks did not reach step 5"):
         gate.wait(5)
-    store.add("torobi_b200/step/6", 1)  # the other rank got there first
+    store.add(gate.key(6), 1)  # the other rank got there first
     gate.wait(6)
     with pytest.raises(ValueError):
         StepGate(store, 0, 2, timeout=0)
+
+
+def test_step_gate_generations_and_key_cleanup():
+    """Each attempt's gates take a fresh generation, so arrivals counted by an
+    earlier attempt (e.g. before a restore) never open a later attempt's gate;
+    a step's key goes once the next step's gate has passed."""
+    import torch.distributed as dist
+
+    from torobi_b200.train import RankLost, StepGate
+
+    store = dist.HashStore()
+    g0, g1 = StepGate(store, 0, 2, timeout=0.2), StepGate(store, 1, 2, timeout=0.2)
+    assert g0.generation == g1.generation == 0
+    store.add(g1.key(0), 1)
+    g0.wait(0)
+    store.add(g1.key(1), 1)
+    g0.wait(1)
+    assert not store.check([g0.key(0)]) and store.check([g0.key(1)])
+    # A second attempt in the same store, at step counts the first one used.
+    h0, h1 = StepGate(store, 0, 2, timeout=0.2), StepGate(store, 1, 2, timeout=0.2)
+    assert h0.generation == h1.generation == 1
+    with pytest.raises(RankLost):
+        h0.wait(1)  # the first attempt's two arrivals at step 1 do not count
+
+
+class _GlooReduce:
+    """The trainer's reduce interface over gloo: launch, then watch."""
+
+    def __init__(self, rank):
+        self.rank, self.works, self.aborted = rank, [], False
+
+    def __call__(self, t):
+        import torch.distributed as dist
+
+        self.works.append(dist.all_reduce(t, async_op=True))
+
+    def watch(self, timeout):
+        from torobi_b200.train import RankLost, wait_collective
+
+        def error():
+            for w in self.works:
+                if w.is_completed() and not w.is_success():
+                    return "gloo work failed"
+            return None
+
+        try:
+            wait_collective(lambda: all(w.is_completed() for w in self.works), error, timeout,
+                            self.rank, "the gradient allreduce")
+        except RankLost:
+            self.aborted = True
+            raise
+        self.works.clear()
+
+
+def _collective_worker(rank, world, init, out_dir, die_after_gate):
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
+    from torobi_b200.train import RankLost, StepGate
+
+    dist.init_process_group("gloo", init_method=init, rank=rank, world_size=world)
+    gate = StepGate(dist.distributed_c10d._get_default_store(), rank, world, timeout=2.0)
+    red = _GlooReduce(rank)
+    result = "ok"
+    t0 = time.monotonic()
+    try:
+        for step in range(3):
+            gate.wait(step)
+            if rank == 1 and step == die_after_gate:
+                (Path(out_dir) / "r1.txt").write_text("died")
+                os._exit(0)  # past the gate, before its allreduce
+            t = torch.ones(4)
+            red(t)
+            red.watch(gate.timeout)
+            assert t[0].item() == world
+    except RankLost:
+        result = f"lost {time.monotonic() - t0:.2f} aborted={red.aborted}"
+    (Path(out_dir) / f"r{rank}.txt").write_text(result)
+    os._exit(0)
+
+
+@pytest.mark.parametrize("die_after_gate", [-1, 1])
+def test_a_rank_lost_after_the_gate_is_caught_in_the_collective_wait(die_after_gate):
+    """Rank 1 checks in at step 1's gate and then exits before its allreduce:
+    rank 0's allreduce can never finish, and the host-side wait under the
+    gate's deadline reports RankLost (the reduce aborted) instead of hanging."""
+    import torch.multiprocessing as mp
+
+    with tempfile.TemporaryDirectory() as d:
+        init = f"tcp://127.0.0.1:{_free_port()}"
+        ctx = mp.get_context("spawn")
+        procs = [ctx.Process(target=_collective_worker, args=(r, 2, init, d, die_after_gate))
+                 for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(90)
+            if p.exitcode is None:
+                p.kill()
+            assert p.exitcode == 0
+        r0 = (Path(d) / "r0.txt").read_text()
+        r1 = (Path(d) / "r1.txt").read_text()
+    if die_after_gate < 0:
+        assert (r0, r1) == ("ok", "ok")
+    else:
+        assert r1 == "died"
+        assert r0.startswith("lost") and r0.endswith("aborted=True"), r0
+        assert float(r0.split()[1]) < 30.0

@@ -82,6 +82,66 @@ def test_loss_matches_f32_reference(cuda, tied):
     assert abs(want - math.log(cfg.vocab)) < 2.0  # near uniform at random init
 
 
+def _random_adapters(model, std):
+    """Non-zero B so the adapter contributes to the loss."""
+    for ad in model.store.adapters.values():
+        ad.b.normal_(0.0, std)
+    model.store.refresh_bf16(full=True)
+
+
+@pytest.mark.gpu
+def test_loss_matches_f32_reference_llama3_8b_widths(cuda):
+    """The Llama-3-8B-shaped model's exact widths (hidden 4096, 32/8 heads of
+    128, SwiGLU 14336, untied 128256 vocabulary, theta 5e5, LoRA r16 alpha 32
+    on all seven projections, 4-bit g64), two layers deep, on 2 x 2048 tokens:
+    the loss within 1e-3 relative of the f32 restatement."""
+    import dataclasses
+
+    import torch
+
+    from torobi_b200.model import LLAMA3_8B, QLoRACausalLM
+
+    cfg = dataclasses.replace(LLAMA3_8B, layers=2)
+    model = QLoRACausalLM(cfg, cuda, seed=21)
+    _random_adapters(model, 0.01)
+    g = torch.Generator(device=cuda)
+    g.manual_seed(5)
+    ids = torch.randint(0, cfg.vocab, (2, 2048), generator=g, device=cuda)
+    with torch.no_grad():
+        got = float(model.loss(ids))
+        want = float(_f32_reference_loss(model, ids))
+    del model
+    torch.cuda.empty_cache()
+    assert abs(got - want) / want < 1e-3, (got, want)
+
+
+@pytest.mark.gpu
+def test_loss_matches_f32_reference_qwen2_5_0_5b(cuda):
+    """The Qwen2.5-0.5B-shaped model whole: 24 layers, hidden 896, 14/2 heads
+    of 64, SwiGLU 4864, tied 151936 vocabulary, q/k/v biases, theta 1e6, LoRA
+    r8 alpha 16 on q and v, 4-bit g64; batch 8 x 512: the loss within 1e-3
+    relative of the f32 restatement."""
+    import torch
+
+    from torobi_b200.model import QWEN2_5_0_5B, QLoRACausalLM
+
+    cfg = QWEN2_5_0_5B
+    model = QLoRACausalLM(cfg, cuda, seed=22)
+    _random_adapters(model, 0.01)
+    for blk in model.blocks:  # non-zero q/k/v biases so they count
+        for name in ("q_proj", "k_proj", "v_proj"):
+            blk.linears[name].bias.normal_(0.0, 0.02)
+    g = torch.Generator(device=cuda)
+    g.manual_seed(6)
+    ids = torch.randint(0, cfg.vocab, (8, 512), generator=g, device=cuda)
+    with torch.no_grad():
+        got = float(model.loss(ids))
+        want = float(_f32_reference_loss(model, ids))
+    del model
+    torch.cuda.empty_cache()
+    assert abs(got - want) / want < 1e-3, (got, want)
+
+
 @pytest.mark.gpu
 def test_adapter_gradients_match_f32_reference(cuda):
     """bf16 activations against an f32 graph: compared norm-wise (a few bf16

@@ -229,3 +229,51 @@ def test_trainable_share_of_qwen_r8_qv(oracle):
     per_layer = r * hidden + hidden * r + r * hidden + kv_dim * r
     assert 2 * 2 * layers == 96
     assert per_layer * layers == 540_672
+
+
+def test_decoder_restatement_vjps_match_torch_autograd():
+    """The CPU decoder restatement (the timed CPU baseline) differentiates
+    RMSNorm, RoPE, causal GQA attention and SwiGLU as torch autograd does in
+    f32, to the bf16 rounding of its outputs."""
+    import numpy as np
+    import torch
+
+    from oracle import decoder as D
+
+    rng = np.random.default_rng(0)
+    T, Hq, Hk, Dh = 12, 4, 2, 16
+    f = lambda *s: D.rb(rng.standard_normal(s, dtype=np.float32))  # noqa: E731
+
+    def close(a, b, tol=2e-2):
+        a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+        return np.max(np.abs(a - b)) <= tol * max(1e-6, np.max(np.abs(b)))
+
+    x, w, dy = f(T, 64), f(64), f(T, 64)
+    y, rstd = D.rms_norm(x, w, 1e-6)
+    xt = torch.tensor(x, requires_grad=True)
+    yt = xt * torch.rsqrt(xt.pow(2).mean(-1, keepdim=True) + 1e-6) * torch.tensor(w)
+    yt.backward(torch.tensor(dy))
+    assert close(y, yt.detach().numpy()) and close(D.rms_norm_vjp(x, w, rstd, dy), xt.grad)
+
+    q, k, v, do = f(T, Hq, Dh), f(T, Hk, Dh), f(T, Hk, Dh), f(T, Hq, Dh)
+    o, p = D.attention(q, k, v)
+    qt, kt, vt = (torch.tensor(a, requires_grad=True) for a in (q, k, v))
+    ot = torch.nn.functional.scaled_dot_product_attention(
+        qt.transpose(0, 1), kt.transpose(0, 1), vt.transpose(0, 1), is_causal=True,
+        enable_gqa=True).transpose(0, 1)
+    ot.backward(torch.tensor(do))
+    assert close(o, ot.detach().numpy())
+    for mine, ref in zip(D.attention_vjp(q, k, v, p, do), (qt.grad, kt.grad, vt.grad)):
+        assert close(mine, ref)
+
+    cos, sin = D.rope_tables(T, Dh, 1e4)
+    r = D.rope(q, cos, sin)
+    assert close(D.rope(r, cos, sin, inverse=True), q)  # a rotation: VJP = inverse
+
+    g, u, da = f(T, 32), f(T, 32), f(T, 32)
+    gt, ut = torch.tensor(g, requires_grad=True), torch.tensor(u, requires_grad=True)
+    at = torch.nn.functional.silu(gt) * ut
+    at.backward(torch.tensor(da))
+    dg, du = D.swiglu_vjp(g, u, da)
+    assert close(D.swiglu(g, u), at.detach().numpy())
+    assert close(dg, gt.grad) and close(du, ut.grad)

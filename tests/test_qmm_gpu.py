@@ -153,3 +153,74 @@ def test_split_k_matches_the_unsplit_kernel(cuda):
                                       n, k, 1, 64, 4, y1.data_ptr(), ws.data_ptr(),
                                       nbytes.value - 16, st)
     assert rc != 0 and b"workspace" in lib().tq_last_error()
+
+
+# The quantized_matmul shape sweep: Llama-3-8B projections (4096x4096,
+# 1024x4096, 14336x4096, 4096x14336) and Llama-3-70B ones (8192x8192,
+# 28672x8192, 8192x28672) as (w_rows, w_cols), 4-bit group 64, weights
+# N(0, 0.02), x and dY N(0, 1), at every token count of the sweep.  Above 256
+# tokens the oracle is evaluated on a sample of token rows that touches every
+# token tile (every 37th row and the last two), which keeps it to seconds;
+# the kernel still computes the whole product.  Operands are drawn on the
+# device (seeded) and the oracle gets the same bf16 values.
+SWEEP_SHAPES = [(4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336), (8192, 8192),
+                (28672, 8192), (8192, 28672)]
+SWEEP_MS = [16, 128, 1024, 4096, 16384]
+_SWEEP_CACHE: dict = {}
+
+
+def _sweep_weight(oracle, cuda, n, k):
+    """Seeded weight of one sweep shape, quantized by the oracle; cached
+    (host and device copies) across the cases of that shape."""
+    import torch
+
+    from _util import host_bf16
+
+    key = (n, k)
+    if key not in _SWEEP_CACHE:
+        _SWEEP_CACHE.clear()  # one shape's operands at a time
+        g = torch.Generator(device=cuda)
+        g.manual_seed(1000 + n + k)
+        w = host_bf16((torch.randn(n, k, device=cuda, generator=g) * 0.02).bfloat16())
+        c, s, b = oracle.quantize(w, 4, 64)
+        del w
+        _SWEEP_CACHE[key] = ((c, s, b), (dev_u32(c, cuda), dev_bf16(s, cuda), dev_bf16(b, cuda)))
+    return _SWEEP_CACHE[key]
+
+
+def _sample_rows(m):
+    if m <= 256:
+        return np.arange(m)
+    return np.array(sorted(set(range(0, m, 37)) | {m - 2, m - 1}))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("direction", ["fwd", "dx"])
+@pytest.mark.parametrize("m", SWEEP_MS)
+@pytest.mark.parametrize("shape", SWEEP_SHAPES, ids=lambda s: "n{}_k{}".format(*s))
+def test_quantized_matmul_projection_sweep(cuda, oracle, shape, m, direction):
+    import torch
+    import torobi_b200 as tq
+
+    from _util import host_bf16
+
+    n, k = shape
+    (c, s, b), (dc, ds, db) = _sweep_weight(oracle, cuda, n, k)
+    g = torch.Generator(device=cuda)
+    g.manual_seed(7 * m + (1 if direction == "dx" else 0))
+    inner, n_out = (k, n) if direction == "fwd" else (n, k)
+    x = torch.randn(m, inner, device=cuda, generator=g).bfloat16()
+    y = tq.quantized_matmul(x, dc, ds, db, transpose=direction == "fwd", group_size=64, bits=4)
+    assert y.shape == (m, n_out)
+    rows = _sample_rows(m)
+    idx = torch.from_numpy(rows).to(cuda)
+    xs = host_bf16(x.index_select(0, idx))
+    got = y.index_select(0, idx).float().cpu().numpy()
+    del x, y
+    if direction == "fwd":
+        want = oracle.qmm_fwd(xs, c, s, b, 4, 64)
+    else:
+        want = oracle.qmm_dx(xs, c, s, b, 4, 64)
+    assert np.isfinite(got).all()
+    err = oracle.rel_err(got, want)
+    assert err <= TOL, f"max rel err {err:.3e} over {len(rows)} sampled rows"

@@ -4,11 +4,15 @@ allocates.  It is for callers that cannot call cudaMalloc while they run (a
 runtime with no device allocator of its own, or one whose memory belongs to a
 pool this code may not draw from).
 
-Checked through the C ABI against tq_quantized_matmul_ws, the same GEMM with a
-caller-allocated workspace, on two calls in a row of different shapes (the
-second call's partials overwrite the first's in the shared array), within the
-1e-2 max-relative-error bar of the other quantized GEMM tests.  This file is
-named so that pytest collects it last.
+Checked through the C ABI, on calls in a row of different shapes (each
+call's partials overwrite the previous call's in the shared array; the first
+call splits the widest, so partials it leaves behind would be read by a later
+call that failed to write its own):
+- bit for bit against tq_quantized_matmul_ws, the same plan and kernels with a
+  caller-allocated workspace;
+- against the oracle within the 1e-2 max-relative-error bar of the other
+  quantized GEMM tests.
+This file is named so that pytest collects it last.
 """
 from __future__ import annotations
 
@@ -22,10 +26,12 @@ from _util import dev_bf16, dev_u32
 TOL = 1e-2
 LIMIT = 8 << 20  # TQ_NOALLOC_SCRATCH_BYTES
 
-# (m, w_rows, w_cols, transpose, bits, group): both plan a split on a B200.
+# (m, w_rows, w_cols, transpose, bits, group): each plans a split on a B200.
 CALLS = [
-    (16, 4096, 4096, 1, 4, 64),   # forward, one decode-sized batch
-    (100, 2048, 2048, 0, 8, 32),  # the input gradient, 8-bit codes
+    (200, 2048, 4096, 1, 4, 64),   # forward, the largest scratch of the three
+    (16, 1024, 8192, 1, 4, 64),    # forward, many k-splits of a decode-sized batch
+    (100, 2048, 2048, 0, 8, 32),   # the input gradient, 8-bit codes
+    (200, 2048, 4096, 1, 4, 64),   # the first call again, after the others
 ]
 
 
@@ -35,16 +41,16 @@ def _workspace_bytes(L, m, n, k, transpose, bits, group):
     return b.value
 
 
-def _operands(oracle, seed, m, n, k, transpose, bits, group, cuda):
+def _operands(oracle, seed, m, n, k, transpose, bits, group):
     rng = np.random.default_rng(seed)
     x = oracle.normal_bf16(rng, (m, k if transpose else n))
     w = oracle.normal_bf16(rng, (n, k), 0.02)
     c, s, b = oracle.quantize(w, bits, group)
-    return dev_bf16(x, cuda), dev_u32(c, cuda), dev_bf16(s, cuda), dev_bf16(b, cuda)
+    return x, c, s, b
 
 
 @pytest.mark.gpu
-def test_noalloc_matches_the_workspace_entry_point(cuda, oracle):
+def test_noalloc_matches_the_workspace_entry_point_and_the_oracle(cuda, oracle):
     import torch
 
     from torobi_b200._lib import lib
@@ -54,7 +60,8 @@ def test_noalloc_matches_the_workspace_entry_point(cuda, oracle):
     for i, (m, n, k, tr, bits, group) in enumerate(CALLS):
         need = _workspace_bytes(L, m, n, k, tr, bits, group)
         assert 0 < need <= LIMIT, f"call {i} should split within the fixed array ({need} bytes)"
-        x, c, s, b = _operands(oracle, 40 + i, m, n, k, tr, bits, group, cuda)
+        hx, hc, hs, hb = _operands(oracle, 40 + i, m, n, k, tr, bits, group)
+        x, c, s, b = dev_bf16(hx, cuda), dev_u32(hc, cuda), dev_bf16(hs, cuda), dev_bf16(hb, cuda)
         n_out = n if tr else k
         ws = torch.empty(need, dtype=torch.uint8, device=cuda)
         want = torch.empty(m, n_out, dtype=torch.bfloat16, device=cuda)
@@ -67,10 +74,11 @@ def test_noalloc_matches_the_workspace_entry_point(cuda, oracle):
                                            m, n, k, tr, group, bits, got.data_ptr(), stream)
         assert rc == 0, L.tq_last_error().decode()
         torch.cuda.synchronize()
-        g, w = got.float().cpu().numpy(), want.float().cpu().numpy()
-        assert np.isfinite(g).all(), f"call {i}: output not fully written"
-        err = oracle.rel_err(g, w)
-        assert err <= TOL, f"call {i}: max rel err {err:.3e} against tq_quantized_matmul_ws"
+        assert torch.equal(got, want), f"call {i}: differs from tq_quantized_matmul_ws"
+        ref = (oracle.qmm_fwd(hx, hc, hs, hb, bits, group) if tr
+               else oracle.qmm_dx(hx, hc, hs, hb, bits, group))
+        err = oracle.rel_err(got.float().cpu().numpy(), ref)
+        assert err <= TOL, f"call {i}: max rel err {err:.3e} against the oracle"
     status = ctypes.c_int()
     assert L.tq_device_status(ctypes.byref(status), 1) == 0, L.tq_last_error().decode()
 

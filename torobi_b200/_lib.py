@@ -101,6 +101,7 @@ SIGNATURES = {
     "tq_dp_allreduce_sum": ([_vp, _vp, _i64, _i32, _vp], _i32),
     "tq_dp_comm_destroy": ([_vp], _i32),
     "tq_dp_comm_abort": ([_vp], _i32),
+    "tq_dp_comm_async_error": ([_vp, ctypes.POINTER(_i32)], _i32),
 }
 
 _LIB = None

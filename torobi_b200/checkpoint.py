@@ -167,7 +167,10 @@ def save(trainer, directory, seed: int = 0, step: int | None = None, run=None) -
     """Writes the run's state to ``directory`` atomically; returns it.
 
     Everything on the device is synchronised first (the tensors are copied
-    to the host)."""
+    to the host), and the trainer's last step is settled, so a step whose
+    gradient norm was not finite (skipped on the device) is not counted in
+    the optimizer step count the checkpoint records."""
+    trainer.settle()
     d = Path(directory)
     staging = d.with_name(d.name + ".writing")
     if staging.exists():

@@ -63,3 +63,16 @@ extern "C" int tq_dp_comm_abort(void* comm) {
   if (!comm) return TQ_OK;
   return check_nccl(ncclCommAbort(static_cast<ncclComm_t>(comm)), "ncclCommAbort");
 }
+
+// The communicator's asynchronous error state (ncclCommGetAsyncError): the
+// host polls it, with the collective's completion, while it waits for a
+// collective under a deadline.
+extern "C" int tq_dp_comm_async_error(void* comm, int* nccl_result) {
+  if (!comm || !nccl_result) return tq::fail(TQ_ERR_INVALID, "null pointer");
+  ncclResult_t r = ncclSuccess;
+  const int rc = check_nccl(ncclCommGetAsyncError(static_cast<ncclComm_t>(comm), &r),
+                            "ncclCommGetAsyncError");
+  if (rc) return rc;
+  *nccl_result = static_cast<int>(r);
+  return TQ_OK;
+}

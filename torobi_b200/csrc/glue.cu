@@ -229,6 +229,12 @@ int grid_for(int64_t items, int block, int per_sm = 8) {
 
 bool a16(const void* p) { return p == nullptr || aligned(p, 16); }
 
+// Whether the byte ranges [a, a + n) and [b, b + n) share a byte.
+bool overlap(const void* a, const void* b, size_t n) {
+  const uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+  return x < y + n && y < x + n;
+}
+
 }  // namespace
 }  // namespace tq
 
@@ -261,6 +267,13 @@ extern "C" int tq_add_rmsnorm_fwd(const void* x, const void* res, const void* w,
   if (!x || !res || !w || !s || !y) return fail(TQ_ERR_INVALID, "add_rmsnorm: null pointer");
   if (!a16(x) || !a16(res) || !a16(w) || !a16(s) || !a16(y) || (rstd && !aligned(rstd, 4)))
     return fail(TQ_ERR_MISALIGNED, "add_rmsnorm: x, res, w, s and y must be 16-byte aligned");
+  // The kernel forms s = x + res, then reads x and res again for the norm of
+  // s: an s or y written over either input would be summed twice.
+  const size_t bytes = static_cast<size_t>(rows) * static_cast<size_t>(hidden) * 2;
+  if (overlap(s, x, bytes) || overlap(s, res, bytes) || overlap(y, x, bytes) ||
+      overlap(y, res, bytes) || overlap(y, s, bytes))
+    return fail(TQ_ERR_INVALID,
+                "add_rmsnorm: s and y must not overlap x, res or each other (no in-place form)");
   const int warps = 8;
   const unsigned grid = static_cast<unsigned>((rows + warps - 1) / warps);
   rmsnorm_fwd_kernel<true><<<grid, warps * 32, 0, as_stream(stream)>>>(

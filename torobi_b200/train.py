@@ -86,6 +86,29 @@ class NcclGradReduce:
         check(lib().tq_dp_allreduce_sum(self.comm, buf.data_ptr(), buf.numel(), TQ_DTYPE_F32,
                                         torch.cuda.current_stream().cuda_stream))
 
+    def watch(self, timeout: float) -> None:
+        """Waits on the host, at most ``timeout`` seconds, for the collectives
+        launched so far on the current stream.  A peer that died after the
+        step's gate leaves its allreduce unfinished for good: on NCCL's
+        asynchronous error, or when the deadline passes, the communicator is
+        aborted (its kernels then return) and ``RankLost`` is raised."""
+        if self.world == 1 or self.comm is None:
+            return
+        ev = torch.cuda.Event()
+        ev.record()
+        code = ctypes.c_int(0)
+
+        def error():
+            check(lib().tq_dp_comm_async_error(self.comm, ctypes.byref(code)))
+            # ncclInProgress (7) is a non-blocking communicator's normal state.
+            return None if code.value in (0, 7) else f"NCCL async error {code.value}"
+
+        try:
+            wait_collective(ev.query, error, timeout, self.rank, "the gradient allreduce")
+        except RankLost:
+            self.abort()
+            raise
+
     def close(self) -> None:
         if self.comm is not None:
             check(lib().tq_dp_comm_destroy(self.comm))
@@ -104,18 +127,45 @@ class RankLost(RuntimeError):
     launched, so no rank is left waiting inside NCCL."""
 
 
-class StepGate:
-    """Host-side liveness check before each step's collectives.
+def wait_collective(done, error, timeout: float, rank: int, what: str) -> None:
+    """Polls ``done()`` until it is true; raises ``RankLost`` when ``error()``
+    returns a message or ``timeout`` seconds pass first."""
+    deadline = time.monotonic() + timeout
+    pause = 0.0002
+    while True:
+        finished = done()
+        # Checked after completion too: a collective can end in an error.
+        msg = error()
+        if msg:
+            raise RankLost(f"rank {rank}: {what} failed ({msg}); a peer is gone")
+        if finished:
+            return
+        if time.monotonic() > deadline:
+            raise RankLost(f"rank {rank}: {what} did not finish within {timeout:g} s; "
+                           f"a peer is gone")
+        time.sleep(pause)
+        pause = min(pause * 2, 0.01)
 
-    Every rank checks in under the step's key of the torch.distributed store
-    (one ``add``) and waits, polling, until all ``world`` ranks have; a rank
-    that has not arrived within ``timeout`` seconds is reported as lost with
-    ``RankLost``.  An NCCL allreduce whose peer has died never returns, so the
-    check is made before the allreduce is launched: the surviving ranks leave
-    the step between kernels, with nothing of theirs in flight.  The reference
-    has one process and nothing like this (its runtime poisons itself on a
-    panic, engine/src/runtime.rs:105-117); it is the data-parallel form of
-    "a failed step does not hang the next one".
+
+class StepGate:
+    """Host-side liveness check around each step's collectives.
+
+    Before: every rank checks in under the step's key of the torch.distributed
+    store (one ``add``) and waits, polling, until all ``world`` ranks have; a
+    rank that has not arrived within ``timeout`` seconds is reported as lost
+    with ``RankLost``, before any collective of the step is launched.  After:
+    a trainer with a gate waits for the step's allreduce on the host under the
+    same deadline (``NcclGradReduce.watch``), so a peer that dies between the
+    gate and the collective is reported too, with the communicator aborted.
+    The reference has one process and nothing like this (its runtime poisons
+    itself on a panic, engine/src/runtime.rs:105-117); it is the data-parallel
+    form of "a failed step does not hang the next one".
+
+    Keys carry a generation: the gates of one attempt of a run (one per rank)
+    take the next generation from a join counter in the store, so a run that
+    is restarted or restored in the same store never counts arrivals left by
+    the attempt before it.  A step's key is deleted once the next step's gate
+    has passed (every rank is then past it).
     """
 
     def __init__(self, store, rank: int, world: int, timeout: float = 240.0,
@@ -123,12 +173,17 @@ class StepGate:
         if timeout <= 0:
             raise ValueError(f"timeout must be positive, got {timeout}")
         self.store, self.rank, self.world = store, rank, world
-        self.timeout, self.prefix = float(timeout), prefix
+        self.timeout = float(timeout)
+        self.generation = (store.add(f"{prefix}/joined", 1) - 1) // world if world > 1 else 0
+        self.prefix = f"{prefix}/g{self.generation}"
+
+    def key(self, step: int) -> str:
+        return f"{self.prefix}/{step}"
 
     def wait(self, step: int) -> None:
         if self.world == 1:
             return
-        key = f"{self.prefix}/{step}"
+        key = self.key(step)
         arrived = self.store.add(key, 1)
         deadline = time.monotonic() + self.timeout
         pause = 0.0005
@@ -139,6 +194,11 @@ class StepGate:
             time.sleep(pause)
             pause = min(pause * 2, 0.05)
             arrived = self.store.add(key, 0)
+        if self.rank == 0 and step > 0:
+            try:
+                self.store.delete_key(self.key(step - 1))
+            except Exception:  # noqa: BLE001  (a store without deletion keeps the key)
+                pass
 
 
 @dataclass
@@ -231,6 +291,10 @@ class Trainer:
                 raise
         self.reduce(st.grads)
         self.reduce(self.loss_buf)
+        if self.gate is not None:
+            watch = getattr(self.reduce, "watch", None)
+            if watch is not None:
+                watch(self.gate.timeout)  # RankLost (communicator aborted) if a peer died
         self.loss_buf /= float(self.world * len(parts))
         ops.sumsq(st.grads, self.norm_sq)
         o = self.opt
