@@ -68,7 +68,8 @@ def _fake(seed=0):
     model = SimpleNamespace(cfg=cfg, embed=torch.randn(cfg.vocab, cfg.hidden, generator=g).bfloat16(),
                             final_norm=torch.ones(cfg.hidden, dtype=torch.bfloat16), lm_head=None,
                             blocks=[blk], store=store)
-    return SimpleNamespace(model=model, opt=AdamWConfig(lr=1e-3), t=7, steps=9)
+    return SimpleNamespace(model=model, opt=AdamWConfig(lr=1e-3), t=7, steps=9,
+                           settle=lambda: float("nan"))
 
 
 def test_save_read_restore_round_trip(tmp_path):

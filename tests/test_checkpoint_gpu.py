@@ -89,3 +89,22 @@ def test_save_replaces_an_older_checkpoint_whole(cuda, tmp_path):
     checkpoint.save(tr, d)
     assert checkpoint.read_manifest(d)["optimizer_steps"] == 1
     assert sorted(p.name for p in tmp_path.iterdir()) == ["ckpt"]
+
+
+@pytest.mark.gpu
+def test_save_right_after_a_skipped_step_counts_only_taken_steps(cuda, tmp_path):
+    """A step whose gradient norm is not finite is skipped on the device
+    (engine/src/state.rs:360-370); a checkpoint written straight after it,
+    before anything read the norm back, records the steps actually taken."""
+    from torobi_b200 import checkpoint
+
+    model, tr, ids = _run(cuda)
+    tr.step(ids)
+    tr.settle()
+    a = next(iter(model.store.adapters.values()))
+    a.a[0, 0] = float("nan")  # the next loss and gradients are NaN
+    model.store.refresh_bf16(full=True)
+    tr.step(ids)  # launched, not settled
+    d = checkpoint.save(tr, tmp_path / "ckpt")
+    assert checkpoint.read_manifest(d)["optimizer_steps"] == 1
+    assert tr.t == 1
