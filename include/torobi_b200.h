@@ -145,8 +145,10 @@ int tq_quantized_matmul(const void* x, const void* codes, const void* scales, co
  *   transpose == 0:  y = x . W + lora_down . lora_up
  *                    lora_up = LoRA A [rank, w_cols]   (bias must be NULL)
  * lora_down is the caller's [m, rank] bf16 down-projection, already scaled
- * by alpha/rank (tq_lora_down).  rank in {8, 16}; lora_up/lora_down NULL
- * (rank 0) leaves the plain GEMM.
+ * by alpha/rank (tq_lora_down), with row pitch ld_down elements (0 = rank;
+ * otherwise a multiple of 8 >= rank): the columns of one adapter inside the
+ * stacked down-projection of linears that share x.  rank in {8, 16};
+ * lora_up/lora_down NULL (rank 0) leaves the plain GEMM.
  * Replaces the node chain matmul, add, matmul, matmul, mul_scalar, add of
  * lib/torobi/dsl/layers.rb:22-24 and lib/torobi/lora.rb:79-85, dispatched at
  * engine/src/interp.rs:192,198,247,270.
@@ -154,7 +156,7 @@ int tq_quantized_matmul(const void* x, const void* codes, const void* scales, co
 int tq_qlora_matmul(const void* x, const void* codes, const void* scales, const void* biases,
                     int64_t m, int64_t w_rows, int64_t w_cols, int transpose, int group_size,
                     int bits, const void* bias, const void* lora_up, const void* lora_down,
-                    int64_t rank, void* y, void* stream);
+                    int64_t ld_down, int64_t rank, void* y, void* stream);
 
 /*
  * Split-K forms of the two GEMM entry points.  When the output tiles alone
@@ -176,8 +178,8 @@ int tq_quantized_matmul_ws(const void* x, const void* codes, const void* scales,
 int tq_qlora_matmul_ws(const void* x, const void* codes, const void* scales, const void* biases,
                        int64_t m, int64_t w_rows, int64_t w_cols, int transpose, int group_size,
                        int bits, const void* bias, const void* lora_up, const void* lora_down,
-                       int64_t rank, void* y, void* workspace, size_t workspace_bytes,
-                       void* stream);
+                       int64_t ld_down, int64_t rank, void* y, void* workspace,
+                       size_t workspace_bytes, void* stream);
 
 /*
  * tq_quantized_matmul with no workspace argument and no allocation: the

@@ -40,8 +40,13 @@ def test_host_side_argument_errors_need_no_gpu():
     assert rc == TQ_ERR_UNSUPPORTED and b"bits" in L.tq_last_error()
     rc = L.tq_quantized_matmul(dummy, dummy, dummy, dummy, 4, 12, 64, 1, 64, 4, dummy, None)
     assert rc == TQ_ERR_INVALID and b"multiple of 8" in L.tq_last_error()
-    rc = L.tq_qlora_matmul(dummy, dummy, dummy, dummy, 4, 16, 64, 1, 64, 4, None, dummy, dummy, 4,
-                           dummy, None)
+    rc = L.tq_qlora_matmul(dummy, dummy, dummy, dummy, 4, 16, 64, 1, 64, 4, None, dummy, dummy, 0,
+                           4, dummy, None)
+    assert rc == TQ_ERR_UNSUPPORTED and b"rank" in L.tq_last_error()
+    rc = L.tq_qlora_matmul(dummy, dummy, dummy, dummy, 4, 16, 64, 1, 64, 4, None, dummy, dummy, 12,
+                           8, dummy, None)
+    assert rc == TQ_ERR_INVALID and b"ld_down" in L.tq_last_error()
+    rc = L.tq_lora_down(dummy, dummy, 4, 64, 72, 1.0, dummy, None, 0, None)
     assert rc == TQ_ERR_UNSUPPORTED and b"rank" in L.tq_last_error()
     rc = L.tq_adamw(dummy, dummy, dummy, dummy, 10, 0, 0.1, 0.9, 0.999, 1e-8, 0.0, 1.0, None, 0.0,
                     None, None)

@@ -170,3 +170,105 @@ def test_lora_down_with_k_split_over_a_cluster(cuda, oracle, m, k, r):
     g_ref = (x.float().t() @ out_t[:, :m].float().t()).cpu().numpy()
     err = oracle.rel_err(g.cpu().numpy(), g_ref)
     assert err <= 1e-4, f"grad: max rel err {err:.3e}"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,k,r", [(8192, 4096, 48),   # q/k/v stacked, r16 each
+                                   (8192, 4096, 32),   # gate/up stacked
+                                   (4096, 896, 16),    # Qwen q/v, r8 each
+                                   (300, 320, 24),     # three r8 adapters, ragged rows
+                                   (520, 1024, 64)])   # the widest stack
+def test_stacked_down_projection_and_gradient(cuda, oracle, m, k, r):
+    """Several adapters' A matrices stacked along the rank (linears that read
+    one x): the down-projection of all of them in one pass equals the f32
+    reference, each member's columns bit-equal to its own single-adapter
+    launch; the stacked gradient P^T.x equals the f32 product."""
+    import torch
+    import torobi_b200 as tq
+
+    torch.manual_seed(13)
+    x = torch.randn(m, k, device=cuda).bfloat16()
+    a = (torch.randn(r, k, device=cuda) / 8).bfloat16()
+    out, out_t = tq.lora_down(x, a, 2.0)
+    want = (2.0 * (x.float() @ a.float().t())).cpu().numpy()
+    assert oracle.rel_err(out.float().cpu().numpy(), want) <= TOL
+    assert torch.equal(out_t[:, :m], out.t())
+    width = 8 if r % 16 else 16
+    for c0 in range(0, r, width):
+        one, _ = tq.lora_down(x, a[c0:c0 + width].contiguous(), 2.0)
+        assert torch.equal(one, out[:, c0:c0 + width]), c0
+    g = tq.lora_grad(x, out_t, 1)
+    g_ref = (out_t[:, :m].float() @ x.float()).cpu().numpy()
+    assert oracle.rel_err(g.cpu().numpy(), g_ref) <= 1e-4
+    # The backward writes each member's transposed rows into its slice.
+    buf = torch.zeros(r, out_t.shape[1], dtype=torch.bfloat16, device=cuda)
+    for c0 in range(0, r, width):
+        tq.lora_down(x, a[c0:c0 + width].contiguous(), 2.0, out_t=buf[c0:c0 + width])
+    assert torch.equal(buf[:, :m], out_t[:, :m])
+
+
+@pytest.mark.gpu
+def test_gemm_reads_an_adapter_s_columns_of_a_stacked_down_projection(cuda):
+    """qlora_matmul given a column slice of a stacked [m, R] down-projection
+    (row pitch R) equals the call on a contiguous copy of those columns, bit
+    for bit, on the single-CTA, split-K and pair paths."""
+    import torch
+    import torobi_b200 as tq
+
+    torch.manual_seed(17)
+    for m, n, k in ((300, 1032, 1024), (32, 1024, 2048), (1536, 3072, 2560)):
+        w = (torch.randn(n, k, device=cuda) * 0.02).bfloat16()
+        c, s, b = tq.quantize(w, 64, 4)
+        x = torch.randn(m, k, device=cuda).bfloat16()
+        stack = torch.randn(m, 48, device=cuda).bfloat16()
+        up = (torch.randn(n, 16, device=cuda) * 0.05).bfloat16()
+        for c0 in (0, 16, 32):
+            got = tq.qlora_matmul(x, c, s, b, True, 64, 4, lora_up=up,
+                                  lora_down=stack[:, c0:c0 + 16])
+            want = tq.qlora_matmul(x, c, s, b, True, 64, 4, lora_up=up,
+                                   lora_down=stack[:, c0:c0 + 16].contiguous())
+            assert torch.equal(got, want), (m, n, k, c0)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("targets", [("q_proj", "k_proj", "v_proj"), ("q_proj", "v_proj")])
+def test_grouped_linears_match_one_linear_at_a_time(cuda, targets):
+    """qlora_linears over q/k/v (one stacked down-projection and one dA pass)
+    gives the outputs of three qlora_linear calls bit for bit, and the same
+    input gradient and adapter gradients to summation order."""
+    import torch
+
+    from torobi_b200.qlora import LoRAStore, QuantizedWeight, qlora_linear, qlora_linears
+
+    torch.manual_seed(19)
+    d_in, outs = 512, {"q_proj": 512, "k_proj": 128, "v_proj": 128}
+    ws = [QuantizedWeight.from_dense((torch.randn(o, d_in, device=cuda) * 0.02).bfloat16(),
+                                     4, 64, torch.randn(o, device=cuda).bfloat16())
+          for o in outs.values()]
+    stores = []
+    for grouped in (True, False):
+        st = LoRAStore(cuda)
+        for name, o in outs.items():
+            if name in targets:
+                st.declare(name, d_in, o, 16, 32.0, group="qkv" if grouped else None)
+        st.materialize(torch.Generator(device=cuda).manual_seed(3))
+        for ad in st.adapters.values():
+            ad.b.normal_(0.0, 0.05, generator=torch.Generator(device=cuda).manual_seed(4))
+        st.refresh_bf16(full=True)
+        stores.append(st)
+    x = torch.randn(2, 96, d_in, device=cuda).bfloat16()
+    dys = [torch.randn(2, 96, o, device=cuda).bfloat16() for o in outs.values()]
+    res = []
+    for st, grouped in zip(stores, (True, False)):
+        ads = [st.adapters.get(n) for n in outs]
+        xi = x.clone().requires_grad_()
+        ys = qlora_linears(xi, ws, ads) if grouped else [qlora_linear(xi, w, ad)
+                                                          for w, ad in zip(ws, ads)]
+        torch.autograd.backward(ys, dys)
+        res.append((ys, xi.grad, st.grads.clone()))
+    (y1, dx1, g1), (y2, dx2, g2) = res
+    assert len(stores[0].groups) == 1 and not stores[1].groups
+    for a, b in zip(y1, y2):
+        assert torch.equal(a, b)
+    assert ((dx1.float() - dx2.float()).abs().max() / dx2.float().abs().max()).item() < 1e-2
+    assert ((g1 - g2).abs().max() / g2.abs().max()).item() < 1e-4

@@ -1,9 +1,11 @@
 // The LoRA side branch's skinny products on the tensor cores.
 //
-// Both are GEMMs with a 16-wide side (rank 8 or 16; rank 8 zero-padded by the
-// TMA out-of-bounds fill), so they are HBM-bound on streaming the big operand
-// once.  One kernel serves both: a 128-row tile of the big operand on the
-// UMMA's M side (TMEM lanes), the rank on its N side (16 columns).
+// Both are GEMMs with a narrow side (the rank: 8 or 16 for one adapter, up to
+// 64 for the adapters of linears that share an input, e.g. q/k/v, stacked;
+// padded to NB = 16, 32 or 64 by the TMA out-of-bounds fill), so they are
+// HBM-bound on streaming the big operand once.  One kernel serves both: a
+// 128-row tile of the big operand on the UMMA's M side (TMEM lanes), the rank
+// on its N side (NB columns).
 //
 //   down  (A K-major):  D[i, j] = sum_k x[i, k] * a[j, k]           i over rows of x
 //   grad  (A MN-major): D[c, j] = sum_m x[m, c] * p_t[j, m]         c over columns of x
@@ -31,23 +33,29 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;  // one 128-byte swizzle atom of the reduction per TMA box
 constexpr int kThreads = 192;
 constexpr int kABytes = kBM * kBK * 2;  // 16 KB
-constexpr int kBBytes = 16 * kBK * 2;   // 2 KB
 constexpr int kMaxSplit = 4;
-constexpr int kPartBytes = kBM * 16 * 4;  // one CTA's f32 partial tile, 8 KB
+constexpr int kMaxRank = 64;
 
-// Shared-memory map: kStages stages of [A tile | B tile], the barrier area
-// (256 bytes), then down's partials of cluster ranks 1..split-1.  (Stages of
-// two or four 64-wide atoms, 256 or 512 contiguous bytes per row, ran no
-// faster: the row tiles already stream near the HBM copy rate.)
-constexpr int kStages = 8;
-constexpr int kStageBytes = kABytes + kBBytes;
-constexpr int kBarsOff = kStages * kStageBytes;
-constexpr int kPartsOff = kBarsOff + 256;
-constexpr int kSmem = 1024 + kPartsOff;
-constexpr int kSmemMax = kSmem + (kMaxSplit - 1) * kPartBytes;
-static_assert(8 * (2 * kStages + 2) <= 256, "barrier area");
-static_assert(kSmemMax <= 232448, "shared memory per CTA");
-static_assert(kStageBytes % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
+// Shared-memory map for an NB-wide rank side: STAGES stages of [A tile |
+// B tile], the barrier area (256 bytes), then down's partials of cluster
+// ranks 1..split-1 (128 x NB f32 each).  (Stages of two or four 64-wide atoms,
+// 256 or 512 contiguous bytes per row, ran no faster: the row tiles already
+// stream near the HBM copy rate.)
+template <int NB>
+struct SkinnyCfg {
+  static constexpr int B_BYTES = NB * kBK * 2;
+  static constexpr int STAGES = NB == 16 ? 8 : (NB == 32 ? 7 : 5);
+  static constexpr int STAGE_BYTES = kABytes + B_BYTES;
+  static constexpr int BARS_OFF = STAGES * STAGE_BYTES;
+  static constexpr int PARTS_OFF = BARS_OFF + 256;
+  static constexpr int PART_BYTES = kBM * NB * 4;
+  static constexpr int SMEM = 1024 + PARTS_OFF;
+  static constexpr int SMEM_MAX = SMEM + (kMaxSplit - 1) * PART_BYTES;
+  static constexpr int TMEM_COLS = NB < 32 ? 32 : NB;
+  static_assert(8 * (2 * STAGES + 2) <= 256, "barrier area");
+  static_assert(SMEM_MAX <= 232448, "shared memory per CTA");
+  static_assert(STAGE_BYTES % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
+};
 
 struct SkinnyParams {
   int rows;        // down: m (rows of x); grad: c (columns of x)
@@ -64,22 +72,26 @@ struct SkinnyParams {
   int* status;
 };
 
-template <bool GRAD>
+template <bool GRAD, int NB>
 __global__ void __launch_bounds__(kThreads, 1)
     skinny_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                   const SkinnyParams p) {
+  using C = SkinnyCfg<NB>;
+  constexpr int kStages = C::STAGES;
+  constexpr int kStageBytes = C::STAGE_BYTES;
+  constexpr int kPartBytes = C::PART_BYTES;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* const gbase = smem_raw + (base - raw);
   auto a_s = [&](int s) { return base + s * kStageBytes; };
   auto b_s = [&](int s) { return base + s * kStageBytes + kABytes; };
-  const uint32_t bars = base + kBarsOff;
+  const uint32_t bars = base + C::BARS_OFF;
   auto full_b = [&](int s) { return bars + 8u * s; };
   auto empty_b = [&](int s) { return bars + 8u * (kStages + s); };
   const uint32_t acc_b = bars + 8u * (2 * kStages);
   const uint32_t tmem_slot = bars + 8u * (2 * kStages + 1);
-  const uint32_t parts = base + kPartsOff;  // down with split > 1: ranks 1..split-1
+  const uint32_t parts = base + C::PARTS_OFF;  // down with split > 1: ranks 1..split-1
   volatile uint32_t* tmem_slot_ptr =
       reinterpret_cast<volatile uint32_t*>(gbase + (tmem_slot - base));
 
@@ -103,7 +115,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 32);
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -138,7 +150,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (elect_one_sync()) {
-      constexpr uint32_t idesc = make_idesc_bf16(kBM, 16, GRAD, false);
+      constexpr uint32_t idesc = make_idesc_bf16(kBM, NB, GRAD, false);
       uint32_t acc = 0;
       bool ok = true;
       for (int i = 0; i < nsteps && ok; ++i) {
@@ -167,16 +179,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool epi = warp >= 2;
   const int q = warp & 3;
   const int r = row0 + q * 32 + lane;
-  uint32_t v[16];
+  uint32_t v[NB];
   bool valid = false;
   if (epi) {
     valid = mbar_wait(acc_b, 0, p.status) && nsteps > 0;
     tc_fence_after();
-    tmem_ld_32x32b_x16(tmem + (static_cast<uint32_t>(q * 32) << 16), v);
+#pragma unroll
+    for (int c = 0; c < NB; c += 16)
+      tmem_ld_32x32b_x16(tmem + (static_cast<uint32_t>(q * 32) << 16) + c,
+                         *reinterpret_cast<uint32_t(*)[16]>(v + c));
     tmem_ld_wait();
     if (!valid) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] = 0u;
+      for (int j = 0; j < NB; ++j) v[j] = 0u;
     }
   }
   if (clustered) {
@@ -187,17 +202,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t crank = cluster_ctarank();  // == blockIdx.y: cluster (1, split, 1)
     if (epi && crank != 0) {
       const uint32_t dst = mapa_shared(
-          parts + (crank - 1) * kPartBytes + static_cast<uint32_t>(q * 32 + lane) * 64u, 0);
+          parts + (crank - 1) * kPartBytes + static_cast<uint32_t>(q * 32 + lane) * (NB * 4u), 0);
 #pragma unroll
-      for (int j = 0; j < 16; j += 4) st_cluster_v4(dst + 4u * j, v[j], v[j + 1], v[j + 2], v[j + 3]);
+      for (int j = 0; j < NB; j += 4) st_cluster_v4(dst + 4u * j, v[j], v[j + 1], v[j + 2], v[j + 3]);
     }
     __syncwarp();
     cluster_sync();
     if (epi && crank == 0) {
       for (int c = 1; c < p.split; ++c) {
-        const uint8_t* src = gbase + (parts - base) + (c - 1) * kPartBytes + (q * 32 + lane) * 64;
+        const uint8_t* src = gbase + (parts - base) + (c - 1) * kPartBytes + (q * 32 + lane) * (NB * 4);
 #pragma unroll
-        for (int j = 0; j < 16; j += 4) {
+        for (int j = 0; j < NB; j += 4) {
           const uint4 w = *reinterpret_cast<const uint4*>(src + 4 * j);
           v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(w.x));
           v[j + 1] = __float_as_uint(__uint_as_float(v[j + 1]) + __uint_as_float(w.y));
@@ -211,28 +226,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (valid && r < p.rows) {
       if constexpr (GRAD) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
+        for (int j = 0; j < NB; ++j) {
           if (j >= p.rank) break;
           float* dst = p.g_layout == 0 ? p.g + static_cast<size_t>(r) * p.rank + j
                                        : p.g + static_cast<size_t>(j) * p.rows + r;
           atomicAdd(dst, __uint_as_float(v[j]));
         }
       } else {
-        uint16_t h[16];
+        uint32_t h2[NB / 2];
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-          h[j] = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[j]) * p.scale));
+        for (int j = 0; j < NB; j += 2)
+          h2[j / 2] = pack_bf16x2_f32(__uint_as_float(v[j]) * p.scale,
+                                      __uint_as_float(v[j + 1]) * p.scale);
+        // The row of out: rank bf16 (a multiple of 8, so whole 16-byte chunks).
         uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<size_t>(r) * p.rank);
-        dst[0] = make_uint4(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16),
-                            h[4] | (uint32_t(h[5]) << 16), h[6] | (uint32_t(h[7]) << 16));
-        if (p.rank == 16)
-          dst[1] = make_uint4(h[8] | (uint32_t(h[9]) << 16), h[10] | (uint32_t(h[11]) << 16),
-                              h[12] | (uint32_t(h[13]) << 16), h[14] | (uint32_t(h[15]) << 16));
+#pragma unroll
+        for (int c8 = 0; c8 < NB / 8; ++c8) {
+          if (c8 * 8 >= p.rank) break;
+          dst[c8] = make_uint4(h2[4 * c8], h2[4 * c8 + 1], h2[4 * c8 + 2], h2[4 * c8 + 3]);
+        }
         if (p.out_t) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
+          for (int j = 0; j < NB; ++j) {
             if (j >= p.rank) break;
-            p.out_t[static_cast<size_t>(j) * p.ld_t + r] = h[j];
+            p.out_t[static_cast<size_t>(j) * p.ld_t + r] =
+                static_cast<uint16_t>(j & 1 ? h2[j / 2] >> 16 : h2[j / 2] & 0xFFFFu);
           }
         }
       }
@@ -244,32 +262,44 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 32);
+    tmem_dealloc(tmem, C::TMEM_COLS);
   }
 }
 
 // Opt in to the large dynamic shared memory (once per device).
-int set_smem_once() {
-  int rc = set_max_smem_once(reinterpret_cast<const void*>(skinny_kernel<false>), kSmemMax,
-                             "cudaFuncSetAttribute(skinny)");
+template <int NB>
+int set_smem_nb() {
+  int rc = set_max_smem_once(reinterpret_cast<const void*>(skinny_kernel<false, NB>),
+                             SkinnyCfg<NB>::SMEM_MAX, "cudaFuncSetAttribute(skinny)");
   if (rc) return rc;
-  return set_max_smem_once(reinterpret_cast<const void*>(skinny_kernel<true>), kSmem,
-                           "cudaFuncSetAttribute(skinny)");
+  return set_max_smem_once(reinterpret_cast<const void*>(skinny_kernel<true, NB>),
+                           SkinnyCfg<NB>::SMEM, "cudaFuncSetAttribute(skinny)");
 }
 
+int set_smem_once() {
+  int rc = set_smem_nb<16>();
+  if (!rc) rc = set_smem_nb<32>();
+  if (!rc) rc = set_smem_nb<64>();
+  return rc;
+}
+
+// The kernel's rank side for a total rank: 16, 32 or 64 columns.
+int rank_width(int64_t rank) { return rank <= 16 ? 16 : (rank <= 32 ? 32 : 64); }
+
 // grid (tiles, split); down with split > 1 runs as clusters (1, split, 1).
-template <bool GRAD>
-int launch_skinny(const CUtensorMap& tm_a, const CUtensorMap& tm_b, const SkinnyParams& p,
-                  int64_t tiles, int64_t split, cudaStream_t stream) {
+template <bool GRAD, int NB>
+int launch_skinny_nb(const CUtensorMap& tm_a, const CUtensorMap& tm_b, const SkinnyParams& p,
+                     int64_t tiles, int64_t split, cudaStream_t stream) {
+  using C = SkinnyCfg<NB>;
   const dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>(split), 1);
   if (GRAD || split == 1) {
-    skinny_kernel<GRAD><<<grid, kThreads, kSmem, stream>>>(tm_a, tm_b, p);
+    skinny_kernel<GRAD, NB><<<grid, kThreads, C::SMEM, stream>>>(tm_a, tm_b, p);
     return check_cuda(cudaGetLastError(), GRAD ? "lora_grad launch" : "lora_down launch");
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = static_cast<size_t>(kSmem + (split - 1) * kPartBytes);
+  cfg.dynamicSmemBytes = static_cast<size_t>(C::SMEM + (split - 1) * C::PART_BYTES);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -278,9 +308,21 @@ int launch_skinny(const CUtensorMap& tm_a, const CUtensorMap& tm_b, const Skinny
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return check_cuda(cudaLaunchKernelEx(&cfg, skinny_kernel<GRAD>, tm_a, tm_b, p),
+  return check_cuda(cudaLaunchKernelEx(&cfg, skinny_kernel<GRAD, NB>, tm_a, tm_b, p),
                     "lora_down launch");
 }
+
+template <bool GRAD>
+int launch_skinny(const CUtensorMap& tm_a, const CUtensorMap& tm_b, const SkinnyParams& p,
+                  int64_t tiles, int64_t split, cudaStream_t stream) {
+  switch (rank_width(p.rank)) {
+    case 16: return launch_skinny_nb<GRAD, 16>(tm_a, tm_b, p, tiles, split, stream);
+    case 32: return launch_skinny_nb<GRAD, 32>(tm_a, tm_b, p, tiles, split, stream);
+    default: return launch_skinny_nb<GRAD, 64>(tm_a, tm_b, p, tiles, split, stream);
+  }
+}
+
+bool rank_ok(int64_t rank) { return rank >= 8 && rank <= kMaxRank && rank % 8 == 0; }
 
 }  // namespace
 }  // namespace tq
@@ -288,7 +330,9 @@ int launch_skinny(const CUtensorMap& tm_a, const CUtensorMap& tm_b, const Skinny
 extern "C" int tq_lora_down(const void* x, const void* a, int64_t m, int64_t k, int64_t rank,
                             float scale, void* out, void* out_t, int64_t ld_t, void* stream) {
   using namespace tq;
-  if (rank != 8 && rank != 16) return fail(TQ_ERR_UNSUPPORTED, "LoRA rank must be 8 or 16, got %lld", (long long)rank);
+  if (!rank_ok(rank))
+    return fail(TQ_ERR_UNSUPPORTED, "LoRA rank (total over stacked adapters) must be a multiple "
+                "of 8 from 8 to %d, got %lld", kMaxRank, (long long)rank);
   if (m < 0 || k < 0) return fail(TQ_ERR_INVALID, "negative shape");
   if (k % 8 != 0) return fail(TQ_ERR_INVALID, "k (%lld) must be a multiple of 8", (long long)k);
   if (m > (1ll << 31) - 1 || k > (1ll << 31) - 1) return fail(TQ_ERR_INVALID, "dimensions must fit in 31 bits");
@@ -320,7 +364,7 @@ extern "C" int tq_lora_down(const void* x, const void* a, int64_t m, int64_t k, 
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(rank)};
     const uint64_t strides[1] = {static_cast<uint64_t>(k) * 2};
-    const uint32_t box[2] = {kBK, 16};
+    const uint32_t box[2] = {kBK, static_cast<uint32_t>(rank_width(rank))};
     rc = encode_tmap(&tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a, dims, strides, box,
                      CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
@@ -357,7 +401,9 @@ extern "C" int tq_lora_down(const void* x, const void* a, int64_t m, int64_t k, 
 extern "C" int tq_lora_grad(const void* x, const void* p_t, int64_t ld_p, int64_t m, int64_t c,
                             int64_t rank, int out_layout, int accumulate, void* g, void* stream) {
   using namespace tq;
-  if (rank != 8 && rank != 16) return fail(TQ_ERR_UNSUPPORTED, "LoRA rank must be 8 or 16, got %lld", (long long)rank);
+  if (!rank_ok(rank))
+    return fail(TQ_ERR_UNSUPPORTED, "LoRA rank (total over stacked adapters) must be a multiple "
+                "of 8 from 8 to %d, got %lld", kMaxRank, (long long)rank);
   if (m < 0 || c < 0) return fail(TQ_ERR_INVALID, "negative shape");
   if (c % 8 != 0) return fail(TQ_ERR_INVALID, "c (%lld) must be a multiple of 8", (long long)c);
   if (ld_p < m || ld_p % 8 != 0)
@@ -392,7 +438,7 @@ extern "C" int tq_lora_grad(const void* x, const void* p_t, int64_t ld_p, int64_
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(m), static_cast<uint64_t>(rank)};
     const uint64_t strides[1] = {static_cast<uint64_t>(ld_p) * 2};
-    const uint32_t box[2] = {kBK, 16};
+    const uint32_t box[2] = {kBK, static_cast<uint32_t>(rank_width(rank))};
     rc = encode_tmap(&tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p_t, dims, strides, box,
                      CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;

@@ -668,6 +668,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace tq
 
 #include "qmm_pair.cuh"
+#include "qmm_pair_ts.cuh"
 
 namespace tq {
 namespace {
@@ -686,6 +687,7 @@ struct Args {
   void* y;
   void* ws = nullptr;        // split-K workspace (f32), or null: no split
   size_t ws_bytes = 0;
+  int64_t ld_down = 0;       // row pitch of lora_down in elements (0: rank)
 };
 
 // How a call is run: the token tile, whether the scale tiles ride in the TMA
@@ -694,6 +696,7 @@ struct Plan {
   int bn = 32;
   bool stma = false;
   bool pair = false;  // two CTAs per 256-row tile (cta_group::2)
+  bool ts = false;    // pair forward with the weight tile in tensor memory
   int splits = 1;
   int k_steps_per_split = 1;
   size_t ws_bytes = 0;
@@ -754,14 +757,27 @@ Plan make_plan(const Args& a, bool allow_split) {
     const char* e = getenv("TQ_QMM_PAIR");
     return e && e[0] == '0';
   }();
+  // The forward runs its pairs with the dequantized weight tile in tensor
+  // memory (token tiles of 192 or 128); TQ_QMM_TS=0 keeps it in shared
+  // memory (token tiles of 256 or 128), for comparison.
+  static const bool ts_off = [] {
+    const char* e = getenv("TQ_QMM_TS");
+    return e && e[0] == '0';
+  }();
   if (!pair_off && pl.stma && pl.splits == 1 && n_out > kBM && aligned(a.y, 16)) {
     const int64_t pair_tiles_n = (n_out + 2 * kBM - 1) / (2 * kBM);
     const int pairs = sm_count() / 2;
     const int forced = forced_bn();
-    for (int cand : {256, 128}) {
-      if ((forced == 256 || forced == 128) && cand != forced) continue;
+    const bool ts = a.transpose && !ts_off;
+    const int top = ts ? 192 : 256;
+    const int cands[2] = {top, 128};
+    for (int cand : cands) {
+      if ((forced == 256 || forced == 192 || forced == 128) &&
+          (forced == 128) != (cand == 128))
+        continue;
       if (a.m >= cand / 2 && ((a.m + cand - 1) / cand) * pair_tiles_n >= pairs) {
         pl.pair = true;
+        pl.ts = ts;
         pl.bn = cand;
         break;
       }
@@ -875,8 +891,9 @@ int make_maps(const Args& a, int x_rows, int sc_rows, bool stma, Maps& mp) {
                        CU_TENSOR_MAP_SWIZZLE_128B);
     }
     if (rc) return rc;
+    const uint64_t ld = static_cast<uint64_t>(a.ld_down ? a.ld_down : a.rank);
     const uint64_t dims[2] = {static_cast<uint64_t>(a.rank), static_cast<uint64_t>(a.m)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(a.rank) * 2};
+    const uint64_t strides[1] = {ld * 2};
     const uint32_t box[2] = {8, static_cast<uint32_t>(BN)};
     rc = encode_tmap(&tm_ldn, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.lora_down, dims, strides, box,
                      CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -1034,8 +1051,52 @@ int launch_pair(const Args& a, const Plan& pl, cudaStream_t stream, int* status)
       "qmm pair launch");
 }
 
+template <int BITS, int BN>
+int launch_pair_ts(const Args& a, const Plan& pl, cudaStream_t stream, int* status) {
+  using C = PairTsCfg<BITS, BN>;
+  Maps mp;
+  int rc = make_maps<BITS, true>(a, BN / 2, C::SC_ROWS, true, mp);
+  if (rc) return rc;
+  const Params p = make_params(a, pl, kPairRows, BN, status);
+  CUtensorMap tm_y;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(a.w_rows), static_cast<uint64_t>(a.m)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(a.w_rows) * 2};
+    const uint32_t box[2] = {32, 32};
+    rc = encode_tmap(&tm_y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.y, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  }
+  auto kernel = qmm_pair_ts_kernel<BITS, BN>;
+  rc = set_max_smem_once(reinterpret_cast<const void*>(kernel), C::SMEM,
+                         "cudaFuncSetAttribute(qmm pair ts smem)");
+  if (rc) return rc;
+  const int pairs = resident_pairs(kernel, C::SMEM);
+  const int grid_pairs = p.tiles_total < pairs ? p.tiles_total : pairs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * grid_pairs, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(C::SMEM);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(
+      cudaLaunchKernelEx(&cfg, kernel, mp.x, mp.c, mp.lup, mp.ldn, mp.sc, mp.bi, tm_y, p),
+      "qmm pair ts launch");
+}
+
 template <int BITS, bool TRANS>
 int launch_bn(const Args& a, const Plan& pl, cudaStream_t stream, int* status) {
+  if constexpr (TRANS) {
+    if (pl.ts)
+      return pl.bn == 192 ? launch_pair_ts<BITS, 192>(a, pl, stream, status)
+                          : launch_pair_ts<BITS, 128>(a, pl, stream, status);
+  }
   if (pl.pair) {
     // Dequantizing groups: two forward (deeper TMA ring), four for dX
     // (measured 0.5-2 % and 3.6-4.8 % better respectively at M >= 8192).
@@ -1067,6 +1128,9 @@ int validate(const Args& a) {
     return fail(TQ_ERR_UNSUPPORTED, "LoRA rank must be 8 or 16 (or 0 for none), got %d", a.rank);
   if (a.rank && (!a.lora_up || !a.lora_down))
     return fail(TQ_ERR_INVALID, "rank %d needs both lora_up and lora_down", a.rank);
+  if (a.rank && a.ld_down != 0 && (a.ld_down < a.rank || a.ld_down % 8 != 0))
+    return fail(TQ_ERR_INVALID, "ld_down (%lld) must be 0 or a multiple of 8 >= rank (%d)",
+                (long long)a.ld_down, a.rank);
   if (!a.transpose && a.bias) return fail(TQ_ERR_INVALID, "bias is only defined for transpose != 0");
   return TQ_OK;
 }
@@ -1120,11 +1184,12 @@ extern "C" int tq_quantized_matmul(const void* x, const void* codes, const void*
 extern "C" int tq_qlora_matmul(const void* x, const void* codes, const void* scales,
                                const void* biases, int64_t m, int64_t w_rows, int64_t w_cols,
                                int transpose, int group_size, int bits, const void* bias,
-                               const void* lora_up, const void* lora_down, int64_t rank, void* y,
-                               void* stream) {
+                               const void* lora_up, const void* lora_down, int64_t ld_down,
+                               int64_t rank, void* y, void* stream) {
   if (rank < 0 || rank > 16) return tq::fail(TQ_ERR_UNSUPPORTED, "LoRA rank must be 8 or 16");
   tq::Args a{x, codes, scales, biases, bias, lora_up, lora_down, m, w_rows, w_cols,
              transpose, group_size, bits, static_cast<int>(rank), y};
+  a.ld_down = ld_down;
   return tq::run(a, stream);
 }
 
@@ -1155,12 +1220,13 @@ extern "C" int tq_quantized_matmul_ws(const void* x, const void* codes, const vo
 extern "C" int tq_qlora_matmul_ws(const void* x, const void* codes, const void* scales,
                                   const void* biases, int64_t m, int64_t w_rows, int64_t w_cols,
                                   int transpose, int group_size, int bits, const void* bias,
-                                  const void* lora_up, const void* lora_down, int64_t rank,
-                                  void* y, void* workspace, size_t workspace_bytes,
-                                  void* stream) {
+                                  const void* lora_up, const void* lora_down, int64_t ld_down,
+                                  int64_t rank, void* y, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
   if (rank < 0 || rank > 16) return tq::fail(TQ_ERR_UNSUPPORTED, "LoRA rank must be 8 or 16");
   tq::Args a{x, codes, scales, biases, bias, lora_up, lora_down, m, w_rows, w_cols,
              transpose, group_size, bits, static_cast<int>(rank), y, workspace, workspace_bytes};
+  a.ld_down = ld_down;
   return tq::run(a, stream);
 }
 

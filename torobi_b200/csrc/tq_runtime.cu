@@ -109,6 +109,18 @@ int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const voi
                 CUtensorMapSwizzle swizzle) {
   int rc = get_encoder();
   if (rc) return rc;
+  // The encoder is a driver call and needs a current context.  A host thread
+  // whose first CUDA work is this call (e.g. a framework's backward worker,
+  // which only selected the device) has none bound yet: binding the runtime's
+  // context to the thread once is what every runtime call would do first.
+  thread_local int bound_dev = -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(TQ_ERR_CUDA, "no current CUDA device");
+  if (bound_dev != dev) {
+    rc = check_cuda(cudaSetDevice(dev), "cudaSetDevice");
+    if (rc) return rc;
+    bound_dev = dev;
+  }
   cuuint64_t gdim[5];
   cuuint64_t gstride[4];
   cuuint32_t bdim[5];

@@ -29,10 +29,20 @@ import torch
 import torch.nn.functional as F
 
 from . import glue
-from .qlora import Adapter, LoRAStore, QuantizedWeight, qlora_linear
+from .qlora import Adapter, LoRAStore, QuantizedWeight, qlora_linear, qlora_linears
 from .weights import linear_path
 
 LINEARS = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+
+# Linears of a block that read the same input: their adapters are stacked so
+# that one pass over that input serves all of them.
+INPUT_GROUPS = {"q_proj": "qkv", "k_proj": "qkv", "v_proj": "qkv", "gate_proj": "gate_up",
+                "up_proj": "gate_up"}
+
+
+def _input_group(layer: int, name: str) -> str | None:
+    g = INPUT_GROUPS.get(name)
+    return f"layers.{layer}.{g}" if g else None
 
 
 @dataclass(frozen=True)
@@ -195,7 +205,7 @@ class QLoRACausalLM:
                 del w
                 if name in cfg.lora_targets:
                     self.store.declare(f"layers.{li}.{name}", d_in, d_out, cfg.lora_rank,
-                                       cfg.lora_alpha)
+                                       cfg.lora_alpha, group=_input_group(li, name))
             self.blocks.append(blk)
         # The adapter's matrices are fresh whatever the source (they are in
         # no published model): A drawn from the seed, B zero.
@@ -230,9 +240,8 @@ class QLoRACausalLM:
         cfg = self.cfg
         B, S, H = x.shape
         cos, sin = self._rope(S)
-        q = qlora_linear(h, blk.linears["q_proj"], blk.adapters["q_proj"])
-        k = qlora_linear(h, blk.linears["k_proj"], blk.adapters["k_proj"])
-        v = qlora_linear(h, blk.linears["v_proj"], blk.adapters["v_proj"])
+        qkv = ("q_proj", "k_proj", "v_proj")
+        q, k, v = qlora_linears(h, [blk.linears[n] for n in qkv], [blk.adapters[n] for n in qkv])
         # [B, S, heads, D] in memory; attention reads the [B, heads, S, D] view.
         q = glue.rope(q.view(B, S, cfg.heads, cfg.head_dim), cos, sin)
         k = glue.rope(k.view(B, S, cfg.kv_heads, cfg.head_dim), cos, sin)
@@ -244,8 +253,8 @@ class QLoRACausalLM:
         x, h = glue.add_rms_norm(x, qlora_linear(att, blk.linears["o_proj"],
                                                  blk.adapters["o_proj"]),
                                  blk.post_norm, cfg.rms_eps)
-        g = qlora_linear(h, blk.linears["gate_proj"], blk.adapters["gate_proj"])
-        u = qlora_linear(h, blk.linears["up_proj"], blk.adapters["up_proj"])
+        gu = ("gate_proj", "up_proj")
+        g, u = qlora_linears(h, [blk.linears[n] for n in gu], [blk.adapters[n] for n in gu])
         return glue.add_rms_norm(x, qlora_linear(glue.swiglu(g, u), blk.linears["down_proj"],
                                                  blk.adapters["down_proj"]),
                                  next_norm, cfg.rms_eps)

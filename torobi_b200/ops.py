@@ -345,6 +345,7 @@ def qlora_matmul(x: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, biase
                                                group_size, bits)
     _need_cuda(op, bias=bias, lora_up=lora_up, lora_down=lora_down)
     rank = 0
+    ld_down = 0
     if lora_up is not None or lora_down is not None:
         if lora_up is None or lora_down is None:
             raise ValueError(f"[{op}] lora_up and lora_down go together")
@@ -358,6 +359,12 @@ def qlora_matmul(x: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, biase
             raise ValueError(f"[{op}] LoRA operands must be bfloat16")
         if rank not in (8, 16):
             raise ValueError(f"[{op}] LoRA rank must be 8 or 16, got {rank}")
+        if lora_down.dim() == 2 and lora_down.stride(1) == 1 and lora_down.stride(0) >= rank:
+            # Columns of a stacked down-projection: read in place, row pitch
+            # stride(0) (the kernel requires it to be a multiple of 8).
+            ld_down = lora_down.stride(0)
+            if ld_down % 8 != 0:
+                raise ValueError(f"[{op}] lora_down's row pitch ({ld_down}) must be a multiple of 8")
     if bias is not None:
         if not transpose:
             raise ValueError(f"[{op}] a bias is only defined with transpose=True")
@@ -365,7 +372,12 @@ def qlora_matmul(x: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, biase
             raise ValueError(f"[{op}] bias must be bfloat16 of shape ({n_out},)")
     y = torch.empty(tuple(x.shape[:-1]) + (n_out,), dtype=torch.bfloat16, device=x.device)
     up = lora_up.contiguous() if lora_up is not None else None
-    down = lora_down.contiguous().reshape(-1, rank) if lora_down is not None else None
+    if lora_down is None:
+        down = None
+    elif ld_down:
+        down = lora_down
+    else:
+        down = lora_down.contiguous().reshape(-1, rank)
     b = bias.contiguous() if bias is not None else None
     with torch.cuda.device(x.device):
         ws, ws_bytes = _workspace(x2.shape[0], w_rows, w_cols, transpose, group_size, bits,
@@ -373,33 +385,48 @@ def qlora_matmul(x: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, biase
         _launch("qmm", lambda: lib().tq_qlora_matmul_ws(
             _ptr(x2), _ptr(w_q.contiguous()), _ptr(scales.contiguous()), _ptr(biases.contiguous()),
             x2.shape[0], w_rows, w_cols, 1 if transpose else 0, group_size, bits, _ptr(b), _ptr(up),
-            _ptr(down), rank, _ptr(y), _ptr(ws), ws_bytes, _stream()),
+            _ptr(down), ld_down, rank, _ptr(y), _ptr(ws), ws_bytes, _stream()),
             2.0 * x2.shape[0] * w_rows * w_cols,
             _qmm_bytes(x2.shape[0], w_rows, w_cols, transpose, group_size, bits))
     return y
 
 
-def lora_down(x: torch.Tensor, a: torch.Tensor, scale: float, want_transposed: bool = True):
+def _lora_rank_ok(rank: int) -> bool:
+    return 8 <= rank <= 64 and rank % 8 == 0
+
+
+def lora_down(x: torch.Tensor, a: torch.Tensor, scale: float, want_transposed: bool = True,
+              out_t: torch.Tensor | None = None):
     """Scaled LoRA down-projection on the tensor cores.
 
     Returns ``(out, out_t)``: ``out`` = RNE(scale * x . a^T) bf16 [m, r] and
     ``out_t`` the same transposed, bf16 [r, ld] with ld = m rounded up to 8
-    (columns m.. unused), or None.
+    (columns m.. unused), or None.  ``a`` may stack the A matrices of several
+    adapters whose linears share x (r up to 64); ``out_t`` may be given (a
+    contiguous [r, ld] bf16 buffer, e.g. rows of a larger stacked one).
     """
     op = "lora_down"
-    _need_cuda(op, x=x, a=a)
+    _need_cuda(op, x=x, a=a, out_t=out_t)
     if x.dtype != torch.bfloat16 or a.dtype != torch.bfloat16:
         raise ValueError(f"[{op}] x and a must be bfloat16")
     rank, k = a.shape
-    if rank not in (8, 16):
-        raise ValueError(f"[{op}] LoRA rank must be 8 or 16, got {rank}")
+    if not _lora_rank_ok(rank):
+        raise ValueError(f"[{op}] LoRA rank must be a multiple of 8 from 8 to 64, got {rank}")
     if x.shape[-1] != k:
         raise ValueError(f"[{op}] x's last dimension ({x.shape[-1]}) must be {k}")
     x2 = x.contiguous().reshape(-1, k)
     m = x2.shape[0]
-    ld = (m + 7) // 8 * 8
     out = torch.empty((m, rank), dtype=torch.bfloat16, device=x.device)
-    out_t = torch.empty((rank, ld), dtype=torch.bfloat16, device=x.device) if want_transposed else None
+    if out_t is not None:
+        ld = out_t.shape[-1]
+        if (out_t.dtype != torch.bfloat16 or not out_t.is_contiguous() or out_t.dim() != 2
+                or out_t.shape[0] != rank or ld < m or ld % 8 != 0):
+            raise ValueError(f"[{op}] out_t must be a contiguous bf16 [{rank}, ld] buffer with "
+                             f"ld >= {m} a multiple of 8, got {tuple(out_t.shape)}")
+    else:
+        ld = (m + 7) // 8 * 8
+        if want_transposed:
+            out_t = torch.empty((rank, ld), dtype=torch.bfloat16, device=x.device)
     with torch.cuda.device(x.device):
         _launch("lora_down", lambda: lib().tq_lora_down(
             _ptr(x2), _ptr(a.contiguous()), m, k, rank, float(scale), _ptr(out), _ptr(out_t), ld,
@@ -417,6 +444,8 @@ def lora_grad(x: torch.Tensor, p_t: torch.Tensor, out_layout: int, out: torch.Te
     op = "lora_grad"
     _need_cuda(op, x=x, p_t=p_t, out=out)
     rank, ld = p_t.shape
+    if not _lora_rank_ok(rank):
+        raise ValueError(f"[{op}] LoRA rank must be a multiple of 8 from 8 to 64, got {rank}")
     c = x.shape[-1]
     x2 = x.contiguous().reshape(-1, c)
     m = x2.shape[0]
