@@ -224,3 +224,46 @@ def test_quantized_matmul_projection_sweep(cuda, oracle, shape, m, direction):
     assert np.isfinite(got).all()
     err = oracle.rel_err(got, want)
     assert err <= TOL, f"max rel err {err:.3e} over {len(rows)} sampled rows"
+
+
+_TS_SCRIPT = r"""
+import sys
+import numpy as np
+sys.path.insert(0, sys.argv[1])
+sys.path.insert(0, sys.argv[1] + "/tests")
+from _util import dev_bf16, dev_u32
+from oracle import oracle
+import torch, torobi_b200 as tq
+cuda = torch.device("cuda", 0)
+worst = 0.0
+for (m, n, k, bits, group) in [(2000, 2304, 2560, 4, 64), (4096, 4096, 4096, 4, 64),
+                               (1100, 3080, 1024, 8, 32), (700, 1024, 2048, 4, 128)]:
+    rng = np.random.default_rng(m + n)
+    x = oracle.normal_bf16(rng, (m, k))
+    c, s, b = oracle.quantize(oracle.normal_bf16(rng, (n, k), 0.02), bits, group)
+    y = tq.quantized_matmul(dev_bf16(x, cuda), dev_u32(c, cuda), dev_bf16(s, cuda),
+                            dev_bf16(b, cuda), True, group, bits)
+    rows = np.arange(0, m, 7)
+    want = oracle.qmm_fwd(np.ascontiguousarray(x[rows]), c, s, b, bits, group)
+    worst = max(worst, oracle.rel_err(y.float().cpu().numpy()[rows], want))
+print(worst)
+"""
+
+
+@pytest.mark.gpu
+def test_tensor_memory_weight_tile_variant(cuda):
+    """The forward pair kernel variant whose dequantized weight tile lives in
+    tensor memory (opt-in, TQ_QMM_TS=1, read once per process, hence the
+    child process) against the oracle, 4- and 8-bit, token tiles 192 and 128
+    with ragged edges."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = str(Path(__file__).resolve().parent.parent)
+    out = subprocess.run([sys.executable, "-c", _TS_SCRIPT, root], capture_output=True,
+                         text=True, timeout=600, env={**os.environ, "TQ_QMM_TS": "1"})
+    assert out.returncode == 0, out.stderr[-2000:]
+    err = float(out.stdout.strip().splitlines()[-1])
+    assert err <= TOL, f"max rel err {err:.3e}"

@@ -757,12 +757,15 @@ Plan make_plan(const Args& a, bool allow_split) {
     const char* e = getenv("TQ_QMM_PAIR");
     return e && e[0] == '0';
   }();
-  // The forward runs its pairs with the dequantized weight tile in tensor
-  // memory (token tiles of 192 or 128); TQ_QMM_TS=0 keeps it in shared
-  // memory (token tiles of 256 or 128), for comparison.
+  // TQ_QMM_TS=1 runs the forward pairs with the dequantized weight tile in
+  // tensor memory (token tiles of 192 or 128).  Off by default: exact, and
+  // it takes the weight tile's store and operand read out of shared memory,
+  // but at 16384 x 4096 x 4096 it ran 1334 TFLOP/s against 1409 for the
+  // shared-memory pairs (the tensor pipe was no busier: 71 % against 74 % of
+  // active cycles), so shared-memory traffic is not what bounds the pairs.
   static const bool ts_off = [] {
     const char* e = getenv("TQ_QMM_TS");
-    return e && e[0] == '0';
+    return !(e && e[0] == '1');
   }();
   if (!pair_off && pl.stma && pl.splits == 1 && n_out > kBM && aligned(a.y, 16)) {
     const int64_t pair_tiles_n = (n_out + 2 * kBM - 1) / (2 * kBM);
