@@ -57,7 +57,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--workload", choices=("llama3-8b", "qwen2.5-0.5b", "qmm", "qmm-sweep",
-                                          "quant-sweep", "lora", "merge", "load"),
+                                          "quant-sweep", "lora", "merge", "load", "attn"),
                    default="llama3-8b")
     p.add_argument("--m", type=int, default=16384, help="qmm: tokens")
     p.add_argument("--n", type=int, default=4096, help="qmm: weight rows (out features)")
@@ -739,6 +739,51 @@ def run_kernels(args):
                                        "peak_kind": f"{peak_kind} copy"},
                           "linears": rows}), flush=True)
         return 0
+    if args.workload == "attn":
+        # Causal grouped-query attention at the two models' head shapes, this
+        # package's tensor-core kernels against the library SDPA (PyTorch's
+        # fused attention) on the same inputs, forward and forward+backward.
+        import torch.nn.functional as F
+
+        from torobi_b200 import glue
+
+        rows = []
+        for name, (b, sq, h, hk, d) in (("llama3-8b", (4, 2048, 32, 8, 128)),
+                                         ("qwen2.5-0.5b", (8, 512, 14, 2, 64))):
+            g = torch.Generator(device=dev)
+            g.manual_seed(0)
+            q = torch.randn(b, sq, h, d, device=dev, generator=g).bfloat16()
+            k = torch.randn(b, sq, hk, d, device=dev, generator=g).bfloat16()
+            v = torch.randn(b, sq, hk, d, device=dev, generator=g).bfloat16()
+            # causal: sq * (sq + 1) / 2 score entries per head, two matmuls
+            flops = 2.0 * 2.0 * b * h * d * sq * (sq + 1) / 2
+
+            def ours():
+                glue.attention_forward(q, k, v, True)
+
+            def lib_sdpa():
+                F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2),
+                                               v.transpose(1, 2), is_causal=True,
+                                               enable_gqa=h != hk)
+
+            ms_o = _time_kernel(ours, K, W, flush)
+            ms_l = _time_kernel(lib_sdpa, K, W, flush)
+            rows.append({"shape": name, "batch": b, "seq": sq, "heads": h, "kv_heads": hk,
+                         "dim": d, "fwd_ms": ms_o, "fwd_tflops": flops / ms_o / 1e9,
+                         "library_fwd_ms": ms_l, "library_fwd_tflops": flops / ms_l / 1e9})
+            print(json.dumps(rows[-1]), file=sys.stderr, flush=True)
+        val = rows[0]["fwd_tflops"]
+        peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+        print(json.dumps({"metric": "causal GQA attention TFLOP/s (Llama-3-8B heads, seq 2048)",
+                          "value": val, "unit": "TFLOP/s", "scaling": "weak", "dtype": "bf16",
+                          **common,
+                          "config": {"workload": "attention forward, 4 x 2048, 32/8 heads of 128",
+                                     "l2": "flushed before every launch (clean)"},
+                          "roofline": {"bound": "tensor", "achieved": val, "peak": peak,
+                                       "unit": "TFLOP/s", "frac": val / peak,
+                                       "peak_kind": f"{peak_kind} burst bf16"},
+                          "shapes": rows}), flush=True)
+        return 0
     if args.workload == "load":
         # Quantize-at-load of a published dense bf16 file (Llama-3-8B shapes,
         # --layers deep, default 2): file -> host -> device -> quantized.
@@ -788,7 +833,7 @@ def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference(args)
-    if args.workload in ("qmm", "qmm-sweep", "quant-sweep", "lora", "merge", "load"):
+    if args.workload in ("qmm", "qmm-sweep", "quant-sweep", "lora", "merge", "load", "attn"):
         return run_kernels(args)
     return run_ours(args)
 

@@ -314,6 +314,24 @@ int tq_swiglu_fwd(const void* g, const void* u, int64_t n, void* a, void* stream
 int tq_swiglu_bwd(const void* g, const void* u, const void* da, int64_t n, void* dg, void* du,
                   void* stream);
 
+/* ------------------------------------------------------------ attention --- */
+
+/*
+ * Scaled dot-product attention with grouped-query heads, the decoder's
+ * attention node (engine/src/interp.rs:405-432: MLX's fused SDPA with a
+ * causal mode and no mask tensor; lib/torobi/models/llama.rb:297-316):
+ *   o[b, i, h, :] = sum_j softmax_j(scale * q[b, i, h, :] . k[b, j, g, :]) v[b, j, g, :]
+ * with g = h / (heads / kv_heads) and, when causal != 0, j <= i only.
+ * q, o [batch, seq, heads, head_dim]; k, v [batch, seq, kv_heads, head_dim];
+ * bf16, contiguous (the projections' [tokens, features] output viewed per
+ * head).  head_dim 64 or 128; heads a multiple of kv_heads.  lse
+ * [batch, heads, seq] f32 receives each query row's natural-log
+ * log-sum-exp of its scaled scores (what the backward reads).
+ */
+int tq_attention_fwd(const void* q, const void* k, const void* v, int64_t batch, int64_t seq,
+                     int64_t heads, int64_t kv_heads, int64_t head_dim, float scale, int causal,
+                     void* out, float* lse, void* stream);
+
 /* --------------------------------------------------------------- export --- */
 
 /*

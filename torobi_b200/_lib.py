@@ -89,6 +89,8 @@ SIGNATURES = {
     "tq_rmsnorm_fwd": ([_vp, _vp, _i64, _i64, _f32, _vp, _vp, _vp], _i32),
     "tq_add_rmsnorm_fwd": ([_vp, _vp, _vp, _i64, _i64, _f32, _vp, _vp, _vp, _vp], _i32),
     "tq_rmsnorm_bwd": ([_vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp], _i32),
+    "tq_attention_fwd": ([_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _vp, _vp, _vp],
+                         _i32),
     "tq_rope": ([_vp, _i64, _i64, _i64, _i64, _vp, _vp, _i32, _vp, _vp], _i32),
     "tq_swiglu_fwd": ([_vp, _vp, _i64, _vp, _vp], _i32),
     "tq_swiglu_bwd": ([_vp, _vp, _vp, _i64, _vp, _vp, _vp], _i32),

@@ -126,6 +126,33 @@ def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
     return _RoPE.apply(x, cos.contiguous(), sin.contiguous(), x.shape[1])
 
 
+def attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
+                      scale: float | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Grouped-query scaled dot-product attention (engine/src/interp.rs:405-432).
+
+    q [batch, seq, heads, dim], k/v [batch, seq, kv_heads, dim] bf16 (dim 64
+    or 128).  Returns o in q's layout and lse [batch, heads, seq] f32 (the
+    natural-log log-sum-exp of each query row's scaled scores)."""
+    _need_cuda("attention", q=q, k=k, v=v)
+    q = _bf16_contig("q", q)
+    k = _bf16_contig("k", k)
+    v = _bf16_contig("v", v)
+    if q.dim() != 4 or k.shape != v.shape or k.dim() != 4:
+        raise ValueError(f"[attention] q {tuple(q.shape)}, k {tuple(k.shape)}, v "
+                         f"{tuple(v.shape)}: want [batch, seq, heads, dim] and equal k/v")
+    b, s, h, d = q.shape
+    if k.shape[0] != b or k.shape[1] != s or k.shape[3] != d:
+        raise ValueError(f"[attention] k {tuple(k.shape)} does not match q {tuple(q.shape)}")
+    hk = k.shape[2]
+    sc = float(scale) if scale is not None else d ** -0.5
+    o = torch.empty_like(q)
+    lse = torch.empty(b, h, s, dtype=torch.float32, device=q.device)
+    _launch("attention", lambda: lib().tq_attention_fwd(
+        _ptr(q), _ptr(k), _ptr(v), b, s, h, hk, d, sc, int(bool(causal)), _ptr(o), _ptr(lse),
+        _stream()))
+    return o, lse
+
+
 class _SwiGLU(torch.autograd.Function):
     @staticmethod
     def forward(ctx, g, u):
