@@ -766,11 +766,28 @@ def run_kernels(args):
                                                v.transpose(1, 2), is_causal=True,
                                                enable_gqa=h != hk)
 
+            do = torch.randn(b, sq, h, d, device=dev, generator=g).bfloat16()
+            o, lse = glue.attention_forward(q, k, v, True)
+            qt, kt, vt = (t.transpose(1, 2).detach().requires_grad_() for t in (q, k, v))
+            ol = F.scaled_dot_product_attention(qt, kt, vt, is_causal=True, enable_gqa=h != hk)
+            dot = do.transpose(1, 2)
+
+            def ours_bwd():
+                glue.attention_backward(q, k, v, o, do, lse, True)
+
+            def lib_bwd():
+                torch.autograd.grad(ol, (qt, kt, vt), dot, retain_graph=True)
+
             ms_o = _time_kernel(ours, K, W, flush)
             ms_l = _time_kernel(lib_sdpa, K, W, flush)
+            ms_ob = _time_kernel(ours_bwd, K, W, flush)
+            ms_lb = _time_kernel(lib_bwd, K, W, flush)
+            # backward: five matmuls of the forward's size (S, dP, dV, dK, dQ)
             rows.append({"shape": name, "batch": b, "seq": sq, "heads": h, "kv_heads": hk,
                          "dim": d, "fwd_ms": ms_o, "fwd_tflops": flops / ms_o / 1e9,
-                         "library_fwd_ms": ms_l, "library_fwd_tflops": flops / ms_l / 1e9})
+                         "library_fwd_ms": ms_l, "library_fwd_tflops": flops / ms_l / 1e9,
+                         "bwd_ms": ms_ob, "bwd_tflops": 2.5 * flops / ms_ob / 1e9,
+                         "library_bwd_ms": ms_lb, "library_bwd_tflops": 2.5 * flops / ms_lb / 1e9})
             print(json.dumps(rows[-1]), file=sys.stderr, flush=True)
         val = rows[0]["fwd_tflops"]
         peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))

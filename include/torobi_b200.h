@@ -332,6 +332,22 @@ int tq_attention_fwd(const void* q, const void* k, const void* v, int64_t batch,
                      int64_t heads, int64_t kv_heads, int64_t head_dim, float scale, int causal,
                      void* out, float* lse, void* stream);
 
+/*
+ * Its VJP: dq, dk, dv (the layouts of q, k, v) from the upstream gradient
+ * dout and the forward's out and lse, for the same shape, scale and mode
+ * (MLX differentiates its fused SDPA for the reference,
+ * engine/src/executor.rs:163-191).  dk and dv sum over the query heads that
+ * share a key/value head; no atomics, so the result is deterministic.
+ * workspace: tq_attention_bwd_workspace_bytes() bytes of device memory,
+ * 256-byte aligned (two f32 statistics per query row).
+ */
+int tq_attention_bwd_workspace_bytes(int64_t batch, int64_t seq, int64_t heads, size_t* bytes);
+int tq_attention_bwd(const void* q, const void* k, const void* v, const void* out,
+                     const void* dout, const float* lse, int64_t batch, int64_t seq,
+                     int64_t heads, int64_t kv_heads, int64_t head_dim, float scale, int causal,
+                     void* dq, void* dk, void* dv, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
 /* --------------------------------------------------------------- export --- */
 
 /*

@@ -15,7 +15,10 @@ LSE_TOL = 2e-3
 
 
 def _rel(a, b):
-    return ((a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-30)).item()
+    """max |err| / max |ref|, the denominator floored at 1e-3: a gradient
+    that is exactly zero in exact arithmetic (one position: softmax is 1, so
+    dq = dk = 0) comes out as rounding noise of order 1e-7."""
+    return ((a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-3)).item()
 
 
 def reference_attention(q, k, v, causal: bool, scale: float):
@@ -101,3 +104,67 @@ def test_attention_argument_errors(cuda):
     q = torch.zeros(1, 8, 3, 64, dtype=torch.bfloat16, device=cuda)
     with pytest.raises(TqError, match="multiple of kv_heads"):
         glue.attention_forward(q, q[:, :, :2].contiguous(), q[:, :, :2].contiguous())
+
+
+def _reference_grads(q, k, v, do, causal, scale):
+    import torch
+
+    qf, kf, vf = (t.detach().float().requires_grad_() for t in (q, k, v))
+    b, s, h, d = q.shape
+    g = h // k.shape[2]
+    kk = kf.transpose(1, 2).repeat_interleave(g, dim=1)
+    vv = vf.transpose(1, 2).repeat_interleave(g, dim=1)
+    sc = (qf.transpose(1, 2) @ kk.transpose(-1, -2)) * scale
+    if causal:
+        mask = torch.ones(s, s, dtype=torch.bool, device=q.device).triu(1)
+        sc = sc.masked_fill(mask, float("-inf"))
+    o = (torch.softmax(sc, -1) @ vv).transpose(1, 2)
+    return torch.autograd.grad(o, (qf, kf, vf), do.float())
+
+
+BWD_CASES = [
+    (2, 256, 4, 2, 64, True),
+    (1, 300, 4, 1, 128, True),      # ragged
+    (2, 200, 2, 2, 128, False),     # no mask, ragged
+    (1, 1, 2, 1, 64, True),
+    (2, 512, 14, 2, 64, True),      # Qwen2.5-0.5B heads
+    (1, 1024, 32, 8, 128, True),    # Llama-3-8B heads
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", BWD_CASES, ids=lambda c: "b{}_s{}_h{}_{}_d{}_{}".format(
+    *c[:5], "causal" if c[5] else "full"))
+def test_attention_backward(cuda, case):
+    """dq, dk, dv through the autograd op against autograd of the f32
+    restatement (dk/dv summed over the query heads of each group)."""
+    import torch
+
+    from torobi_b200 import glue
+
+    b, s, h, hk, d, causal = case
+    q, k, v = _inputs(cuda, 21 + s, b, s, h, hk, d)
+    g = torch.Generator(device=cuda)
+    g.manual_seed(3 + s)
+    do = torch.randn(b, s, h, d, device=cuda, generator=g).bfloat16()
+    qq, kk, vv = (t.clone().requires_grad_() for t in (q, k, v))
+    o = glue.attention(qq, kk, vv, causal)
+    dq, dk, dv = torch.autograd.grad(o, (qq, kk, vv), do)
+    rq, rk, rv = _reference_grads(q, k, v, do, causal, d ** -0.5)
+    for name, got, ref in (("dq", dq, rq), ("dk", dk, rk), ("dv", dv, rv)):
+        assert _rel(got, ref) <= TOL, f"{name}: {_rel(got, ref):.3e}"
+
+
+@pytest.mark.gpu
+def test_attention_backward_is_deterministic(cuda):
+    import torch
+
+    from torobi_b200 import glue
+
+    q, k, v = _inputs(cuda, 9, 2, 384, 8, 2, 128)
+    do = torch.randn_like(q)
+    o, lse = glue.attention_forward(q, k, v, True)
+    first = glue.attention_backward(q, k, v, o, do, lse, True)
+    again = glue.attention_backward(q, k, v, o, do, lse, True)
+    for a, b_ in zip(first, again):
+        assert torch.equal(a, b_)

@@ -91,6 +91,10 @@ SIGNATURES = {
     "tq_rmsnorm_bwd": ([_vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp], _i32),
     "tq_attention_fwd": ([_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _vp, _vp, _vp],
                          _i32),
+    "tq_attention_bwd_workspace_bytes": ([_i64, _i64, _i64, ctypes.POINTER(ctypes.c_size_t)],
+                                         _i32),
+    "tq_attention_bwd": ([_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _i32,
+                          _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp], _i32),
     "tq_rope": ([_vp, _i64, _i64, _i64, _i64, _vp, _vp, _i32, _vp, _vp], _i32),
     "tq_swiglu_fwd": ([_vp, _vp, _i64, _vp, _vp], _i32),
     "tq_swiglu_bwd": ([_vp, _vp, _vp, _i64, _vp, _vp, _vp], _i32),

@@ -8,10 +8,12 @@ second (engine/src/interp.rs:350-388); SwiGLU is ``(g * sigmoid(g)) * u``
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from .ops import _launch, _need_cuda, _ptr, _stream
-from ._lib import lib
+from ._lib import check, lib
 
 
 def _bf16_contig(name: str, t: torch.Tensor) -> torch.Tensor:
@@ -151,6 +153,57 @@ def attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal:
         _ptr(q), _ptr(k), _ptr(v), b, s, h, hk, d, sc, int(bool(causal)), _ptr(o), _ptr(lse),
         _stream()))
     return o, lse
+
+
+def attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor,
+                       do: torch.Tensor, lse: torch.Tensor, causal: bool = True,
+                       scale: float | None = None):
+    """dq, dk, dv of ``attention_forward`` given the upstream gradient do
+    (q's layout) and the forward's o and lse."""
+    _need_cuda("attention", q=q, k=k, v=v, o=o, do=do, lse=lse)
+    q, k, v, o = (_bf16_contig(n, t) for n, t in (("q", q), ("k", k), ("v", v), ("o", o)))
+    do = _bf16_contig("do", do)
+    if o.shape != q.shape or do.shape != q.shape:
+        raise ValueError("[attention] o and do must have q's shape")
+    b, s, h, d = q.shape
+    hk = k.shape[2]
+    if lse.dtype != torch.float32 or tuple(lse.shape) != (b, h, s):
+        raise ValueError(f"[attention] lse must be f32 [{b}, {h}, {s}]")
+    lse = lse.contiguous()
+    sc = float(scale) if scale is not None else d ** -0.5
+    nbytes = ctypes.c_size_t()
+    check(lib().tq_attention_bwd_workspace_bytes(b, s, h, ctypes.byref(nbytes)))
+    ws = torch.empty(max(1, nbytes.value), dtype=torch.uint8, device=q.device)
+    dq = torch.empty_like(q)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
+    _launch("attention", lambda: lib().tq_attention_bwd(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(do), _ptr(lse), b, s, h, hk, d, sc,
+        int(bool(causal)), _ptr(dq), _ptr(dk), _ptr(dv), _ptr(ws), nbytes.value, _stream()))
+    return dq, dk, dv
+
+
+class _Attention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, causal, scale):
+        o, lse = attention_forward(q, k, v, causal, scale)
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.causal, ctx.scale = causal, scale
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, lse = ctx.saved_tensors
+        dq, dk, dv = attention_backward(q, k, v, o, do, lse, ctx.causal, ctx.scale)
+        return dq, dk, dv, None, None
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
+              scale: float | None = None) -> torch.Tensor:
+    """Differentiable grouped-query attention: q [batch, seq, heads, dim],
+    k/v [batch, seq, kv_heads, dim] bf16, output in q's layout; the scale
+    defaults to dim^-1/2 (engine/src/interp.rs:405-432)."""
+    return _Attention.apply(q, k, v, causal, scale)
 
 
 class _SwiGLU(torch.autograd.Function):
