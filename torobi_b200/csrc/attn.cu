@@ -9,26 +9,12 @@
 // the natural-log log-sum-exp of each query row's scaled scores, kept for the
 // backward.  dim is 64 or 128.
 //
-// Forward, one CTA per (128-query tile, head, sequence), heaviest causal tiles
-// first:
-//   warp 0     TMA: the query tile once, key and value tiles through a ring
-//   warp 1     one thread issues every tcgen05 MMA
-//   warp 2     allocates / frees the 512 TMEM columns
-//   warps 4-7  softmax: thread i owns query row i (TMEM lane i)
-// TMEM: two score buffers S (128 f32 columns each), the output accumulator O
-// (dim columns), two probability buffers P (bf16 pairs, 64 columns each).
-//   S_j = Q K_j^T            (A and B from shared memory, K-major)
-//   P_j = exp2(S_j * c - m)  (softmax warps, written back into TMEM)
-//   O  += P_j V_j            (A = P_j from TMEM, B = V_j MN-major)
-// The MMA issues S_{j+1} before waiting for P_j, so the next scores are ready
-// when the softmax warps finish a tile.  The running maximum m is only moved
-// (and O rescaled in TMEM) when a row's maximum grows by more than 2^8: P
-// then stays below 256, exact in f32 and in range for bf16, and the final
-// 1/l uses the same stale m as every P, so the result is unchanged.
+// The forward and the backward kernels are described where they start below.
 #include <cuda_bf16.h>
 
 #include <cmath>
 #include <cstdlib>
+#include <type_traits>
 
 #include "tq_ptx.cuh"
 #include "tq_runtime.h"
@@ -41,6 +27,23 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleLog2 = 8.0f;  // move m only when the row max grows by > 2^8
 
+// 2^x on the FMA pipe, for a share of the softmax's exponentials (the MUFU
+// unit alone would take as long as the tile's MMAs).  Range reduction by the
+// round-to-nearest of x + 1.5 * 2^23 (n = nearest integer, f = x - n in
+// [-0.5, 0.5]), 2^f by a cubic least-squares fit in relative error (fitted for
+// this kernel; max relative error 7.5e-5 in f32, below bf16's 2^-9), and n
+// added to the exponent field.  x is clamped at -125 so that the result stays
+// a normal number.
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -125.0f);
+  const float t = __fadd_rn(x, 12582912.0f);
+  const float f = __fsub_rn(x, __fsub_rn(t, 12582912.0f));
+  float p = fmaf(0.055174145847558975f, f, 0.24261757731437683f);
+  p = fmaf(p, f, 0.6932610869407654f);
+  p = fmaf(p, f, 0.9999275803565979f);
+  return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
+}
+
 struct AttnShape {
   int batch, seq, heads, kv_heads, group, n_tiles;
   int causal;
@@ -48,6 +51,26 @@ struct AttnShape {
 };
 
 // ------------------------------------------------------------------ forward --
+//
+// One CTA per pair of adjacent 128-query tiles (2p, 2p + 1) of one head and
+// sequence, heaviest causal pairs first; both tiles share every key/value
+// tile the pair needs (tile 2p stops one key tile earlier under the mask).
+//   warp 0       TMA: both query tiles once, key and value tiles through a ring
+//   warp 1       one thread issues every tcgen05 MMA
+//   warp 2       allocates / frees the 512 TMEM columns
+//   warps 4-7    softmax of query tile 0 (thread i owns row i, TMEM lane i)
+//   warps 8-11   softmax of query tile 1
+// TMEM: S_0 | S_1 (128 f32 columns each) | O_0 | O_1 (dim columns each).  The
+// softmax writes P_w (bf16 pairs, 64 columns) over the first half of S_w,
+// chunk by chunk after reading it.  MMA issue order per key tile j:
+//   PV_0(j) = O_0 += P_0(j) V_j,  S_0(j+1) = Q_0 K_{j+1}^T,
+//   PV_1(j),                      S_1(j+1)
+// so one tile's next scores are computed while the other tile's softmax
+// runs.  S_w(j+1) overwrites P_w(j) right after PV_w(j) reads it: tcgen05.mma
+// operations issued by one thread execute in issue order.
+// The softmax reads each row twice from TMEM in 32-column chunks (maximum,
+// then exponentials), which keeps the two softmax warpgroups within the
+// 168 registers a 384-thread CTA has per thread.
 
 template <int D>
 struct FwdCfg {
@@ -56,30 +79,31 @@ struct FwdCfg {
   static constexpr int SLAB_BYTES = kTile * 128;  // 128 rows x 64 bf16
   static constexpr int TILE_BYTES = SLABS * SLAB_BYTES;
   static constexpr int STAGES = D == 128 ? 2 : 4;
-  static constexpr int Q_OFF = 0;
-  static constexpr int K_OFF = TILE_BYTES;
+  static constexpr int Q_OFF = 0;  // two query tiles
+  static constexpr int K_OFF = 2 * TILE_BYTES;
   static constexpr int V_OFF = K_OFF + STAGES * TILE_BYTES;
   static constexpr int BAR_OFF = V_OFF + STAGES * TILE_BYTES;
-  // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_ready[2], o_done[2], slot
-  static constexpr int NBAR = 1 + 4 * STAGES + 2 + 2 + 2;
+  // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2],
+  // p_ready[2], o_done[2]; then the TMEM slot
+  static constexpr int NBAR = 1 + 4 * STAGES + 6;
   static constexpr int SMEM = 1024 + BAR_OFF + 8 * (NBAR + 1);
-  static constexpr int S_COL = 0;          // S_b at S_COL + 128 b
-  static constexpr int O_COL = 256;
-  static constexpr int P_COL = 256 + D;    // P_b at P_COL + 64 b
+  static constexpr int S_COL = 0;    // S_w (and P_w) at 128 w
+  static constexpr int O_COL = 256;  // O_w at 256 + D w
   static constexpr int TMEM_COLS = 512;
-  static_assert(P_COL + 128 <= TMEM_COLS, "tensor memory map");
+  static_assert(O_COL + 2 * D <= TMEM_COLS, "tensor memory map");
   static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
 struct FwdParams {
   AttnShape sh;
+  int n_pairs;
   uint16_t* out;
   float* lse;
   int* status;
 };
 
 template <int D>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(384, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
   using C = FwdCfg<D>;
@@ -88,7 +112,7 @@ __global__ void __launch_bounds__(256, 1)
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* const gbase = smem_raw + (base - raw);
-  const uint32_t q_s = base + C::Q_OFF;
+  auto q_s = [&](int w) { return base + C::Q_OFF + w * C::TILE_BYTES; };
   auto k_s = [&](int s) { return base + C::K_OFF + s * C::TILE_BYTES; };
   auto v_s = [&](int s) { return base + C::V_OFF + s * C::TILE_BYTES; };
   const uint32_t bars = base + C::BAR_OFF;
@@ -97,13 +121,13 @@ __global__ void __launch_bounds__(256, 1)
   auto k_empty = [&](int s) { return bars + 8u * (1 + ST + s); };
   auto v_full = [&](int s) { return bars + 8u * (1 + 2 * ST + s); };
   auto v_empty = [&](int s) { return bars + 8u * (1 + 3 * ST + s); };
-  auto s_full = [&](int b) { return bars + 8u * (1 + 4 * ST + b); };
-  auto p_ready = [&](int b) { return bars + 8u * (3 + 4 * ST + b); };
-  // O += P_j V_j completes on o_done(j & 1).  Every barrier used per tile j
-  // comes in two, indexed by j's parity, and phase j >> 1 of one is only
-  // waited on once tile j - 2's has completed: a parity wait is never more
-  // than one phase behind.
-  auto o_done = [&](int b) { return bars + 8u * (5 + 4 * ST + b); };
+  // Per query tile w, each completing once per key tile j (phase j):
+  // s_full (S_w(j) landed), p_ready (P_w(j) written, O_w rescaled), o_done
+  // (PV_w(j) finished).  S_w(j+1) is only issued after p_ready's phase j, so
+  // no waiter is ever two phases behind.
+  auto s_full = [&](int w) { return bars + 8u * (1 + 4 * ST + w); };
+  auto p_ready = [&](int w) { return bars + 8u * (3 + 4 * ST + w); };
+  auto o_done = [&](int w) { return bars + 8u * (5 + 4 * ST + w); };
   const uint32_t tmem_slot = bars + 8u * C::NBAR;
   volatile uint32_t* tmem_slot_ptr =
       reinterpret_cast<volatile uint32_t*>(gbase + (tmem_slot - base));
@@ -113,12 +137,16 @@ __global__ void __launch_bounds__(256, 1)
   const int lane = threadIdx.x & 31;
   const int bh_count = sh.batch * sh.heads;
   const int bh = blockIdx.x % bh_count;
-  const int qt = sh.n_tiles - 1 - static_cast<int>(blockIdx.x / bh_count);
+  const int pair = p.n_pairs - 1 - static_cast<int>(blockIdx.x / bh_count);
   const int b = bh / sh.heads;
   const int h = bh % sh.heads;
   const int hk = h / sh.group;
-  const int q0 = qt * kTile;
-  const int n_kv = sh.causal ? qt + 1 : sh.n_tiles;
+  const int t0 = 2 * pair;                             // first query tile
+  const bool has1 = t0 + 1 < sh.n_tiles;               // second query tile exists
+  const int n_kv0 = sh.causal ? t0 + 1 : sh.n_tiles;  // key tiles of query tile 0
+  const int n_kv1 = has1 ? (sh.causal ? t0 + 2 : sh.n_tiles) : 0;
+  const int n_kv = n_kv0 > n_kv1 ? n_kv0 : n_kv1;
+  auto nkv_of = [&](int w) { return w == 0 ? n_kv0 : n_kv1; };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -128,10 +156,10 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(v_full(s), 1);
       mbar_init(v_empty(s), 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(s_full(i), 1);
-      mbar_init(p_ready(i), 4);
-      mbar_init(o_done(i), 1);
+    for (int w = 0; w < 2; ++w) {
+      mbar_init(s_full(w), 1);
+      mbar_init(p_ready(w), 4);
+      mbar_init(o_done(w), 1);
     }
     fence_mbar_init();
   }
@@ -150,9 +178,10 @@ __global__ void __launch_bounds__(256, 1)
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      mbar_arrive_expect_tx(q_full, C::TILE_BYTES);
-      for (int sl = 0; sl < C::SLABS; ++sl)
-        tma_load_4d(q_s + sl * C::SLAB_BYTES, &tm_q, q_full, sl * 64, h, q0, b);
+      mbar_arrive_expect_tx(q_full, (has1 ? 2 : 1) * C::TILE_BYTES);
+      for (int w = 0; w < (has1 ? 2 : 1); ++w)
+        for (int sl = 0; sl < C::SLABS; ++sl)
+          tma_load_4d(q_s(w) + sl * C::SLAB_BYTES, &tm_q, q_full, sl * 64, h, (t0 + w) * kTile, b);
       int nk = 0, nv = 0;  // tiles issued
       for (int j = 0; j < n_kv; ++j) {
         const int s = j % ST;
@@ -181,144 +210,205 @@ __global__ void __launch_bounds__(256, 1)
       constexpr uint32_t idesc_s = make_idesc_bf16(kTile, kTile, false, false);
       constexpr uint32_t idesc_o = make_idesc_bf16(kTile, D, false, true);
       bool ok = mbar_wait(q_full, 0, p.status);
-      auto issue_s = [&](int j) -> bool {
+      // S_w(j) = Q_w K_j^T into S_w.
+      auto issue_s = [&](int w, int j) {
         const int s = j % ST;
-        if (!mbar_wait(k_full(s), (j / ST) & 1, p.status)) return false;
-        tc_fence_after();
-        const uint32_t d = tmem + C::S_COL + (j & 1) * kTile;
+        const uint32_t d = tmem + C::S_COL + w * kTile;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * C::SLAB_BYTES + (kk & 3) * 32;
-          umma_bf16(d, make_sdesc(q_s + off, 16, 1024, kSw128),
+          umma_bf16(d, make_sdesc(q_s(w) + off, 16, 1024, kSw128),
                     make_sdesc(k_s(s) + off, 16, 1024, kSw128), idesc_s, kk > 0);
         }
-        umma_commit(s_full(j & 1));
-        umma_commit(k_empty(s));
-        return true;
+        umma_commit(s_full(w));
       };
-      if (ok) ok = issue_s(0);
-      int issued_pv = 0;
-      for (int j = 0; j < n_kv && ok; ++j) {
-        if (j + 1 < n_kv && !issue_s(j + 1)) break;
+      // O_w += P_w(j) V_j, P_w from the first 64 columns of S_w.
+      auto issue_pv = [&](int w, int j) {
         const int s = j % ST;
-        ok = mbar_wait(p_ready(j & 1), (j >> 1) & 1, p.status) &&
-             mbar_wait(v_full(s), (j / ST) & 1, p.status);
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t pa = tmem + C::P_COL + (j & 1) * 64;
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)
-          umma_bf16_ts(tmem + C::O_COL, pa + kk * 8,
+          umma_bf16_ts(tmem + C::O_COL + w * D, tmem + C::S_COL + w * kTile + kk * 8,
                        make_sdesc(v_s(s) + kk * 2048, C::SLAB_BYTES, 1024, kSw128), idesc_o,
                        (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(o_done(w));
+      };
+      // Key tile 0: both tiles' scores.
+      if (ok) ok = mbar_wait(k_full(0), 0, p.status);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        if (n_kv1 > 0) issue_s(1, 0);
+        umma_commit(k_empty(0));
+      }
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int s = j % ST;
+        const bool next = j + 1 < n_kv;
+        if (next) {
+          ok = mbar_wait(k_full((j + 1) % ST), ((j + 1) / ST) & 1, p.status);
+          if (!ok) break;
+        }
+        ok = mbar_wait(v_full(s), (j / ST) & 1, p.status);
+        if (!ok) break;
+        for (int w = 0; w < 2 && ok; ++w) {
+          if (j >= nkv_of(w)) continue;
+          ok = mbar_wait(p_ready(w), j & 1, p.status);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv(w, j);
+          if (j + 1 < nkv_of(w)) issue_s(w, j + 1);
+        }
+        if (!ok) break;
         umma_commit(v_empty(s));
-        umma_commit(o_done(j & 1));
-        ++issued_pv;
+        if (next) umma_commit(k_empty((j + 1) % ST));
       }
-      // Nothing may outlive the CTA's TMEM: the last commit covers every MMA.
-      if (issued_pv > 0) {
-        const int t = issued_pv - 1;
-        mbar_wait(o_done(t & 1), (t >> 1) & 1, p.status);
-      }
+      // Nothing may outlive the CTA's TMEM: wait for each tile's last PV.
+      for (int w = 0; w < 2; ++w)
+        if (nkv_of(w) > 0) mbar_wait(o_done(w), (nkv_of(w) - 1) & 1, p.status);
     }
   } else if (warp >= 4) {
     // --------------------------------------------------------- softmax
+    const int w = (warp - 4) >> 2;  // query tile of this warpgroup
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
-    const int qpos = q0 + row;
+    const int qw0 = (t0 + w) * kTile;
+    const int qpos = qw0 + row;
+    const int nk = nkv_of(w);
     const uint32_t lrow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint32_t scol = lrow + C::S_COL + w * kTile;
+    const uint32_t ocol = lrow + C::O_COL + w * D;
     const float c = sh.scale_log2;
     float m = -INFINITY;
     float l = 0.0f;
     bool ok = true;
-    int j = 0;
-    for (; j < n_kv; ++j) {
-      ok = mbar_wait(s_full(j & 1), (j >> 1) & 1, p.status);
+    for (int j = 0; j < nk; ++j) {
+      ok = mbar_wait(s_full(w), j & 1, p.status);
       if (!ok) break;
       tc_fence_after();
-      float sv[kTile];
-      {
-        uint32_t (&r)[kTile] = *reinterpret_cast<uint32_t(*)[kTile]>(sv);
-#pragma unroll
-        for (int q4 = 0; q4 < kTile / 32; ++q4)
-          tmem_ld_32x32b_x32(lrow + C::S_COL + (j & 1) * kTile + q4 * 32,
-                             *reinterpret_cast<uint32_t(*)[32]>(r + q4 * 32));
-        tmem_ld_wait();
-      }
       const int kv0 = j * kTile;
-      if ((sh.causal && kv0 + kTile - 1 > q0) || kv0 + kTile > sh.seq) {
-        int lim = sh.seq - 1 - kv0;  // last valid column of this tile
+      int lim = kTile - 1;  // last column of this key tile that counts for the row
+      if ((sh.causal && kv0 + kTile - 1 > qw0) || kv0 + kTile > sh.seq) {
+        lim = sh.seq - 1 - kv0;
         if (sh.causal && qpos - kv0 < lim) lim = qpos - kv0;
-#pragma unroll
-        for (int i = 0; i < kTile; ++i)
-          if (i > lim) sv[i] = -INFINITY;
       }
-      float mx = sv[0];
+      // Only the diagonal key tile (causal) and the one past seq need a mask:
+      // both passes come in a masked and an unmasked form.
+      const bool masked = lim < kTile - 1 || (sh.causal && kv0 + kTile - 1 > qw0);
+      // Pass 1: the row maximum (eight interleaved chains, then a tree).
+      float m8[8];
 #pragma unroll
-      for (int i = 1; i < kTile; ++i) mx = fmaxf(mx, sv[i]);
-      const float m_tile = mx * c;
-      const float m_new = fmaxf(m, m_tile);
+      for (int e = 0; e < 8; ++e) m8[e] = -INFINITY;
+      auto pass1 = [&](auto mask_tag) {
+        constexpr bool M = decltype(mask_tag)::value;
+#pragma unroll
+        for (int c4 = 0; c4 < kTile / 32; ++c4) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(scol + c4 * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (!M || c4 * 32 + i <= lim) m8[i & 7] = fmaxf(m8[i & 7], __uint_as_float(r[i]));
+        }
+      };
+      if (masked)
+        pass1(std::true_type{});
+      else
+        pass1(std::false_type{});
+      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+      const float m_new = fmaxf(m, mx * c);
       if (j == 0) {
         m = m_new;
       } else if (__any_sync(0xffffffffu, m_new > m + kRescaleLog2)) {
-        // Move m and rescale this row's O (after the previous P V landed).
+        // Move m and rescale this row of O_w.  PV_w(j-1) has finished: S_w(j)
+        // was issued after it.
         const float f = m == -INFINITY ? 0.0f : ex2_approx(m - m_new);
-        ok = mbar_wait(o_done((j - 1) & 1), ((j - 1) >> 1) & 1, p.status);
+        ok = mbar_wait(o_done(w), (j - 1) & 1, p.status);
         if (!ok) break;
         tc_fence_after();
-#pragma unroll
-        for (int c4 = 0; c4 < D / 32; ++c4) {
-          uint32_t o[32];
-          tmem_ld_32x32b_x32(lrow + C::O_COL + c4 * 32, o);
+#pragma unroll 1
+        for (int c4 = 0; c4 < D / 16; ++c4) {
+          uint32_t o[16];
+          tmem_ld_32x32b_x16(ocol + c4 * 16, o);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-          tmem_st_32x32b_x32(lrow + C::O_COL + c4 * 32, o);
+          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+          tmem_st_32x32b_x16(ocol + c4 * 16, o);
         }
         tmem_st_wait();
         l *= f;
         m = m_new;
       }
       const float mref = m == -INFINITY ? 0.0f : m;
-      float rs = 0.0f;
-      uint32_t pk[kTile / 2];
+      // Pass 2: P = exp2(S c - m), three of four exponentials on the MUFU
+      // unit and one on the FMA pipe, written as bf16 pairs over the first
+      // half of S_w (chunk k's 16 columns lie in chunks already read); the
+      // next chunk's load is in flight while one is computed.
+      float a4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      auto pass2 = [&](auto mask_tag) {
+        constexpr bool M = decltype(mask_tag)::value;
+        uint32_t rb[2][32];
+        tmem_ld_32x32b_x32(scol, rb[0]);
+        tmem_ld_wait();
 #pragma unroll
-      for (int i = 0; i < kTile; i += 2) {
-        const float p0 = ex2_approx(fmaf(sv[i], c, -mref));
-        const float p1 = ex2_approx(fmaf(sv[i + 1], c, -mref));
-        rs += p0 + p1;
-        pk[i / 2] = pack_bf16x2_f32(p0, p1);
-      }
-      l += rs;
-      const uint32_t pcol = lrow + C::P_COL + (j & 1) * 64;
-      tmem_st_32x32b_x32(pcol, *reinterpret_cast<uint32_t(*)[32]>(pk));
-      tmem_st_32x32b_x32(pcol + 32, *reinterpret_cast<uint32_t(*)[32]>(pk + 32));
+        for (int c4 = 0; c4 < kTile / 32; ++c4) {
+          if (c4 + 1 < kTile / 32) tmem_ld_32x32b_x32(scol + (c4 + 1) * 32, rb[(c4 + 1) & 1]);
+          const uint32_t(&r)[32] = rb[c4 & 1];
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            const int col = c4 * 32 + i;
+            float p0 = ex2_approx(fmaf(__uint_as_float(r[i]), c, -mref));
+            float p1 = ex2_approx(fmaf(__uint_as_float(r[i + 1]), c, -mref));
+            float p2 = ex2_approx(fmaf(__uint_as_float(r[i + 2]), c, -mref));
+            float p3 = exp2_poly(fmaf(__uint_as_float(r[i + 3]), c, -mref));
+            if (M) {
+              if (col > lim) p0 = 0.0f;
+              if (col + 1 > lim) p1 = 0.0f;
+              if (col + 2 > lim) p2 = 0.0f;
+              if (col + 3 > lim) p3 = 0.0f;
+            }
+            a4[0] += p0;
+            a4[1] += p1;
+            a4[2] += p2;
+            a4[3] += p3;
+            pk[i / 2] = pack_bf16x2_f32(p0, p1);
+            pk[i / 2 + 1] = pack_bf16x2_f32(p2, p3);
+          }
+          tmem_st_32x32b_x16(scol + c4 * 16, pk);
+          if (c4 + 1 < kTile / 32) tmem_ld_wait();
+        }
+      };
+      if (masked)
+        pass2(std::true_type{});
+      else
+        pass2(std::false_type{});
+      l += (a4[0] + a4[1]) + (a4[2] + a4[3]);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_ready(j & 1));
+      if (lane == 0) mbar_arrive(p_ready(w));
     }
-    if (ok && n_kv > 0) ok = mbar_wait(o_done((n_kv - 1) & 1), ((n_kv - 1) >> 1) & 1, p.status);
+    if (ok && nk > 0) ok = mbar_wait(o_done(w), (nk - 1) & 1, p.status);
     tc_fence_after();
-    if (ok) {
+    if (ok && nk > 0) {
       const float inv = l > 0.0f ? 1.0f / l : 0.0f;
       const bool valid = qpos < sh.seq;
       uint16_t* orow = p.out + ((static_cast<size_t>(b) * sh.seq + qpos) * sh.heads + h) * D;
 #pragma unroll
       for (int c4 = 0; c4 < D / 32; ++c4) {
         uint32_t o[32];
-        tmem_ld_32x32b_x32(lrow + C::O_COL + c4 * 32, o);
+        tmem_ld_32x32b_x32(ocol + c4 * 32, o);
         tmem_ld_wait();
-        uint32_t w[16];
+        uint32_t wd[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i)
-          w[i] = pack_bf16x2_f32(__uint_as_float(o[2 * i]) * inv,
-                                 __uint_as_float(o[2 * i + 1]) * inv);
+          wd[i] = pack_bf16x2_f32(__uint_as_float(o[2 * i]) * inv,
+                                  __uint_as_float(o[2 * i + 1]) * inv);
         if (valid) {
           uint4* dst = reinterpret_cast<uint4*>(orow + c4 * 32);
 #pragma unroll
           for (int i = 0; i < 4; ++i)
-            dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+            dst[i] = make_uint4(wd[4 * i], wd[4 * i + 1], wd[4 * i + 2], wd[4 * i + 3]);
         }
       }
       if (valid)
@@ -1045,11 +1135,12 @@ int launch_fwd(const void* q, const void* k, const void* v, const AttnShape& sh,
   if ((rc = map_bshd(&tv, v, sh.batch, sh.seq, sh.kv_heads, D))) return rc;
   FwdParams p{};
   p.sh = sh;
+  p.n_pairs = (sh.n_tiles + 1) / 2;
   p.out = static_cast<uint16_t*>(out);
   p.lse = lse;
   p.status = status;
-  const unsigned grid = static_cast<unsigned>(sh.batch) * sh.heads * sh.n_tiles;
-  attn_fwd_kernel<D><<<grid, 256, C::SMEM, stream>>>(tq_, tk, tv, p);
+  const unsigned grid = static_cast<unsigned>(sh.batch) * sh.heads * p.n_pairs;
+  attn_fwd_kernel<D><<<grid, 384, C::SMEM, stream>>>(tq_, tk, tv, p);
   return check_cuda(cudaGetLastError(), "attention forward launch");
 }
 
