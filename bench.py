@@ -75,6 +75,8 @@ def parse_args():
     p.add_argument("--graph", choices=("auto", "on", "off"), default="auto",
                    help="replay each step's forward/backward as a CUDA graph "
                         "(auto: on for the launch-bound qwen2.5-0.5b step)")
+    p.add_argument("--attention", choices=("native", "library"), default="library",
+                   help="step workloads: this package's attention kernels or PyTorch SDPA")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
@@ -310,7 +312,7 @@ def run_ours(args):
     rows = hi - lo
     if rows % mb:
         mb = rows
-    model = QLoRACausalLM(cfg, dev, seed=1234)
+    model = QLoRACausalLM(cfg, dev, seed=1234, attention=args.attention)
     store = dist.distributed_c10d._get_default_store() if dist else None
     reduce = NcclGradReduce(rank, world, store)
     graph = args.graph == "on" or (args.graph == "auto" and args.workload == "qwen2.5-0.5b")
@@ -436,7 +438,7 @@ def run_ours(args):
             "data": "synthetic (uniform random token ids, random-init weights)",
             "config": {"workload": f"{args.workload} QLoRA train step", "global_batch": gb,
                        "seq_len": seq, "micro_batch": mb, "parallelism": f"dp{world}",
-                       "cuda_graph": graph,
+                       "cuda_graph": graph, "attention": args.attention,
                        "layers": cfg.layers, "quant": f"{cfg.bits}-bit g{cfg.group}",
                        "lora": f"r{cfg.lora_rank} a{int(cfg.lora_alpha)} on "
                                f"{'+'.join(cfg.lora_targets)}",

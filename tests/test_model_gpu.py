@@ -82,6 +82,46 @@ def test_loss_matches_f32_reference(cuda, tied):
     assert abs(want - math.log(cfg.vocab)) < 2.0  # near uniform at random init
 
 
+@pytest.mark.gpu
+def test_native_attention_loss_and_gradients(cuda):
+    """The model with this package's attention kernels (attention="native"):
+    the loss within 1e-3 relative of the f32 restatement, and the adapters'
+    gradients against that restatement's autograd by the bar of the model
+    gradient test (relative norm error < 5e-2, cosine > 0.999)."""
+    import torch
+
+    from torobi_b200.model import QLoRACausalLM, tiny_config
+
+    cfg = tiny_config(heads=8, kv_heads=2, head_dim=64, hidden=512, lora_rank=16,
+                      lora_alpha=32.0, lora_targets=("q_proj", "k_proj", "v_proj", "o_proj"))
+    g = torch.Generator(device=cuda)
+    g.manual_seed(1)
+    ids = torch.randint(0, cfg.vocab, (2, 384), generator=g, device=cuda)
+    model = QLoRACausalLM(cfg, cuda, seed=4, attention="native")
+    for ad in model.store.adapters.values():
+        ad.b.normal_(0.0, 0.02)
+    model.store.refresh_bf16(full=True)
+    model.store.zero_grad()
+    loss = model.loss(ids)
+    loss.backward()
+    with torch.no_grad():
+        want = float(_f32_reference_loss(model, ids))
+    assert abs(float(loss) - want) / want < 1e-3, (float(loss), want)
+    got = {n: (ad.ga.clone(), ad.gb.clone()) for n, ad in model.store.adapters.items()}
+    leaves = {}
+    for n, ad in model.store.adapters.items():
+        a = ad.a.detach().clone().requires_grad_()
+        b = ad.b.detach().clone().requires_grad_()
+        leaves[n] = (a, b)
+        ad.a, ad.b = a, b
+    _f32_reference_loss(model, ids).backward()
+    for n, (a, b) in leaves.items():
+        for mine, ref in ((got[n][0], a.grad), (got[n][1], b.grad)):
+            err = ((mine - ref).norm() / ref.norm()).item()
+            cos = torch.nn.functional.cosine_similarity(mine.flatten(), ref.flatten(), dim=0).item()
+            assert err < 5e-2 and cos > 0.999, (n, err, cos)
+
+
 def _random_adapters(model, std):
     """Non-zero B so the adapter contributes to the loss."""
     for ad in model.store.adapters.values():

@@ -14,9 +14,9 @@ over next-token targets.
 Every linear of every block is a ``QuantizedWeight`` (MLX affine codes) run by
 the tcgen05 quantized GEMM; adapted linears add the fused LoRA branch.  The
 norms (each residual add fused into the norm after it), RoPE and SwiGLU
-between them are fused kernels (``glue``); attention
-(PyTorch SDPA), the bf16 head and the loss are library calls -- they are
-outside the quantized-weight path this package replaces.
+between them are fused kernels (``glue``); attention is this package's
+tensor-core kernels (``attention="native"``) or PyTorch's fused SDPA
+(``"library"``); the bf16 head is a library GEMM.
 The head stays bf16 (a plain library GEMM): QLoRA quantizes the blocks'
 linears and keeps the vocabulary projection in the compute dtype.
 """
@@ -105,6 +105,10 @@ LLAMA3_8B = DecoderConfig(vocab=128256, hidden=4096, intermediate=14336, layers=
 
 PRESETS = {"qwen2.5-0.5b": QWEN2_5_0_5B, "llama3-8b": LLAMA3_8B}
 
+# Causal GQA attention: this package's tensor-core kernels ("native",
+# glue.attention) or PyTorch's fused SDPA ("library").
+ATTENTION_IMPLS = ("native", "library")
+
 
 def tiny_config(**over) -> DecoderConfig:
     """A small model of the same shape family, for tests."""
@@ -152,8 +156,11 @@ class QLoRACausalLM:
     or (``source``) a published model's weights quantized as they load."""
 
     def __init__(self, cfg: DecoderConfig, device: torch.device | str = "cuda", seed: int = 0,
-                 dtype: torch.dtype = torch.bfloat16, source=None):
+                 dtype: torch.dtype = torch.bfloat16, source=None, attention: str = "library"):
+        if attention not in ATTENTION_IMPLS:
+            raise ValueError(f"attention must be one of {ATTENTION_IMPLS}, got {attention!r}")
         self.cfg = cfg
+        self.attention = attention
         self.device = torch.device(device)
         self.dtype = dtype
         gen = torch.Generator(device=self.device)
@@ -217,12 +224,13 @@ class QLoRACausalLM:
 
     @classmethod
     def from_pretrained(cls, cfg: DecoderConfig, path, device: torch.device | str = "cuda",
-                        seed: int = 0) -> "QLoRACausalLM":
+                        seed: int = 0, attention: str = "library") -> "QLoRACausalLM":
         """A published model's safetensors file, every block linear quantized
         on the device as it arrives; the adapter fresh from ``seed``."""
         from .weights import SafetensorsSource
 
-        return cls(cfg, device=device, seed=seed, source=SafetensorsSource(path))
+        return cls(cfg, device=device, seed=seed, source=SafetensorsSource(path),
+                   attention=attention)
 
     def _rope(self, seq: int):
         t = self._rope_cache.get(seq)
@@ -246,10 +254,15 @@ class QLoRACausalLM:
         q = glue.rope(q.view(B, S, cfg.heads, cfg.head_dim), cos, sin)
         k = glue.rope(k.view(B, S, cfg.kv_heads, cfg.head_dim), cos, sin)
         v = v.view(B, S, cfg.kv_heads, cfg.head_dim)
-        att = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2),
-                                             v.transpose(1, 2), is_causal=True,
-                                             enable_gqa=cfg.heads != cfg.kv_heads)
-        att = att.transpose(1, 2).reshape(B, S, cfg.heads * cfg.head_dim)
+        if self.attention == "native":
+            # The tensor-core kernels read [B, S, heads, D] as it stands and
+            # write the output in the layout o_proj reads.
+            att = glue.attention(q, k, v, causal=True).view(B, S, cfg.heads * cfg.head_dim)
+        else:
+            att = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2),
+                                                 v.transpose(1, 2), is_causal=True,
+                                                 enable_gqa=cfg.heads != cfg.kv_heads)
+            att = att.transpose(1, 2).reshape(B, S, cfg.heads * cfg.head_dim)
         x, h = glue.add_rms_norm(x, qlora_linear(att, blk.linears["o_proj"],
                                                  blk.adapters["o_proj"]),
                                  blk.post_norm, cfg.rms_eps)
