@@ -343,7 +343,7 @@ def run_ours(args):
 
     clocks = ClockSampler(local)
     clocks.start()
-    rec = ops.LaunchRecorder(timed=("qmm",))
+    rec = ops.LaunchRecorder(timed=("qmm", "allreduce"))
     ops.set_recorder(rec)
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
@@ -361,7 +361,9 @@ def run_ours(args):
     tokens_per_step = gb * seq
     value = tokens_per_step * K / (ms / 1000.0)
     summ = rec.summary().get("qmm", {"launches": 0, "ms": 0.0, "flops": 0.0, "bytes": 0.0})
-    launches = rec.launches()
+    ar = rec.summary().get("allreduce", {"launches": 0, "ms": 0.0, "bytes": 0.0})
+    # NCCL's allreduce kernel is a library kernel: not counted as this package's.
+    launches = rec.launches() - rec.counts.get("allreduce", 0)
     step_ms_for_share = local_ms
     roofline_timing = "every launch of the timed steps, CUDA events on its stream"
     if graph:
@@ -408,6 +410,23 @@ def run_ours(args):
                "h2d_bytes_per_step": rows * seq * ids_host.element_size() * world,
                "d2h_bytes_per_step": 8 * world}
 
+    ar_alone_ms = None
+    grads_n = model.store.grads.numel()
+    if world > 1:
+        # Every rank takes these collective steps, in the same order.
+        for i in range(4):
+            barrier()
+            a0 = torch.cuda.Event(enable_timing=True)
+            a1 = torch.cuda.Event(enable_timing=True)
+            a0.record()
+            reduce(model.store.grads)
+            a1.record()
+            torch.cuda.synchronize()
+            if i > 0:
+                t = a0.elapsed_time(a1)
+                ar_alone_ms = t if ar_alone_ms is None else min(ar_alone_ms, t)
+        ar_alone_ms = max_over_ranks(ar_alone_ms)
+
     peaks, peak_kind = measured_peaks()
     achieved = summ["flops"] / (summ["ms"] / 1000.0) / 1e12 if summ["ms"] > 0 else 0.0
     peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
@@ -452,6 +471,17 @@ def run_ours(args):
             "gpu_launches": launches,
             "clocks": clk,
         }
+        if world > 1:
+            # The gradient (and loss) allreduce, CUDA events around each NCCL
+            # call on rank 0's stream inside the timed steps (includes any wait
+            # for a slower rank), and the gradient allreduce alone after a
+            # barrier (the collective's own time).
+            line["allreduce"] = {"ms_per_step": ar["ms"] / K, "launches_per_step":
+                                 ar["launches"] / K, "bytes_per_step": ar["bytes"] / K,
+                                 "share_of_step": ar["ms"] / local_ms if local_ms else None,
+                                 "isolated_ms": ar_alone_ms,
+                                 "isolated_bus_gbs": (2.0 * (world - 1) / world * 4.0 *
+                                                      grads_n / ar_alone_ms / 1e6)}
         print(json.dumps(line), flush=True)
     reduce.close()
     if dist:

@@ -83,8 +83,11 @@ class NcclGradReduce:
         if self.world == 1:
             return
         assert buf.dtype == torch.float32 and buf.is_contiguous()
-        check(lib().tq_dp_allreduce_sum(self.comm, buf.data_ptr(), buf.numel(), TQ_DTYPE_F32,
-                                        torch.cuda.current_stream().cuda_stream))
+        from .ops import _launch
+
+        _launch("allreduce", lambda: lib().tq_dp_allreduce_sum(
+            self.comm, buf.data_ptr(), buf.numel(), TQ_DTYPE_F32,
+            torch.cuda.current_stream().cuda_stream), nbytes=4.0 * buf.numel())
 
     def watch(self, timeout: float) -> None:
         """Waits on the host, at most ``timeout`` seconds, for the collectives
