@@ -130,7 +130,7 @@ def test_split_k_matches_the_unsplit_kernel(cuda):
     from torobi_b200._lib import check, lib
 
     torch.manual_seed(3)
-    m, n, k = 24, 2048, 4096
+    m, n, k = 48, 2048, 4096  # above the small-token kernel's 32, so the tiles split k
     w = (torch.randn(n, k, device=cuda) * 0.02).bfloat16()
     c, s, b = tq.quantize(w, 64, 4)
     x = torch.randn(m, k, device=cuda).bfloat16()
@@ -153,6 +153,50 @@ def test_split_k_matches_the_unsplit_kernel(cuda):
                                       n, k, 1, 64, 4, y1.data_ptr(), ws.data_ptr(),
                                       nbytes.value - 16, st)
     assert rc != 0 and b"workspace" in lib().tq_last_error()
+
+
+# The small-token forward (4-bit, up to 32 tokens, k a multiple of 128):
+# weights dequantized in registers for warp-level MMAs, k split over a
+# cluster.  Token counts across the 8-token tiles, a row count that leaves a
+# partial 128-row block, three chunks of k, every group size, and the
+# linear's bias through tq_qlora_matmul with rank 0.
+SMALL_CASES = [
+    # (m, w_rows, w_cols, group, with_bias)
+    (1, 2064, 1024, 64, False),
+    (3, 256, 8192, 32, True),
+    (8, 1024, 384, 128, False),
+    (16, 4096, 4096, 64, True),
+    (21, 2064, 2048, 32, False),
+    (32, 1024, 14336, 64, True),
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", SMALL_CASES, ids=lambda c: "m{}_n{}_k{}_g{}_{}".format(
+    *c[:4], "bias" if c[4] else "nobias"))
+def test_small_token_forward(cuda, oracle, case):
+    import torch
+
+    from torobi_b200._lib import check, lib
+
+    m, n, k, group, with_bias = case
+    x, _, c, s, b = _setup(oracle, 31 + m, m, n, k, 4, group)
+    rng = np.random.default_rng(m)
+    bias = oracle.normal_bf16(rng, (n,), 0.5) if with_bias else None
+    dx, dc, ds, db = dev_bf16(x, cuda), dev_u32(c, cuda), dev_bf16(s, cuda), dev_bf16(b, cuda)
+    dbias = dev_bf16(bias, cuda) if with_bias else None
+    y = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=cuda)
+    check(lib().tq_qlora_matmul(dx.data_ptr(), dc.data_ptr(), ds.data_ptr(), db.data_ptr(), m, n,
+                                k, 1, group, 4, dbias.data_ptr() if with_bias else None, None,
+                                None, 0, 0, y.data_ptr(),
+                                torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    want = oracle.qmm_fwd(x, c, s, b, 4, group)
+    if with_bias:
+        want = want + oracle.f32_from_bf16(bias)[None, :]
+    got = y.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    assert oracle.rel_err(got, want) <= TOL
 
 
 # The quantized_matmul shape sweep: Llama-3-8B projections (4096x4096,

@@ -29,7 +29,7 @@ LIMIT = 8 << 20  # TQ_NOALLOC_SCRATCH_BYTES
 # (m, w_rows, w_cols, transpose, bits, group): each plans a split on a B200.
 CALLS = [
     (200, 2048, 4096, 1, 4, 64),   # forward, the largest scratch of the three
-    (16, 1024, 8192, 1, 4, 64),    # forward, many k-splits of a decode-sized batch
+    (16, 1024, 8192, 0, 4, 64),    # the input gradient of a decode-sized batch, k split
     (100, 2048, 2048, 0, 8, 32),   # the input gradient, 8-bit codes
     (200, 2048, 4096, 1, 4, 64),   # the first call again, after the others
 ]

@@ -669,6 +669,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 #include "qmm_pair.cuh"
 #include "qmm_pair_ts.cuh"
+#include "qmm_small.cuh"
 
 namespace tq {
 namespace {
@@ -700,6 +701,8 @@ struct Plan {
   int splits = 1;
   int k_steps_per_split = 1;
   size_t ws_bytes = 0;
+  bool small = false;  // register-dequant kernel for a handful of tokens
+  int small_cs = 1;    // its CTAs per 128-row block (cluster splitting k)
 };
 
 // TQ_QMM_BN pins the token tile (256, 128, 64 or 32) for tuning runs.
@@ -726,8 +729,37 @@ int pick_bn(int64_t m, int64_t n_out) {
   return 32;
 }
 
+// The small-token forward (qmm_small.cuh): 4-bit codes, no LoRA, k a
+// multiple of 128, rows of 16.  TQ_QMM_SMALL=0 keeps such calls on the
+// tensor-memory kernel, for comparison.
+bool small_ok(const Args& a) {
+  static const bool off = [] {
+    const char* e = getenv("TQ_QMM_SMALL");
+    return e && e[0] == '0';
+  }();
+  return !off && a.transpose && a.bits == 4 && a.m >= 1 && a.m <= kSmallMaxM && a.rank == 0 &&
+         a.w_cols % kSmallChunk == 0 && a.w_rows % 16 == 0 && aligned(a.x, 16) &&
+         aligned(a.y, 16);
+}
+
+// Smallest cluster (1, 2, 4, 8) whose CTAs give every SM two, keeping at
+// least two k-chunks per CTA; at most 4 with 32 tokens (shared memory).
+int small_cluster(const Args& a) {
+  const int64_t blocks = (a.w_rows + kSmallRows - 1) / kSmallRows;
+  const int64_t chunks = a.w_cols / kSmallChunk;
+  const int cap = a.m > 24 ? 4 : kSmallMaxCluster;
+  int cs = 1;
+  while (cs < cap && blocks * cs < 2 * sm_count() && chunks / (2 * cs) >= 2) cs *= 2;
+  return cs;
+}
+
 Plan make_plan(const Args& a, bool allow_split) {
   Plan pl;
+  if (small_ok(a)) {
+    pl.small = true;
+    pl.small_cs = small_cluster(a);
+    return pl;
+  }
   const int64_t n_out = a.transpose ? a.w_rows : a.w_cols;
   const int64_t k_red = a.transpose ? a.w_cols : a.w_rows;
   pl.bn = pick_bn(a.m, n_out);
@@ -1115,6 +1147,76 @@ int launch_bn(const Args& a, const Plan& pl, cudaStream_t stream, int* status) {
   }
 }
 
+template <int MT>
+int launch_small_mt(const Args& a, const Plan& pl, cudaStream_t stream, int* status) {
+  using C = SmallCfg<MT>;
+  int rc = set_max_smem_once(reinterpret_cast<const void*>(qmm_small_kernel<MT>),
+                             C::smem(kSmallMaxCluster), "cudaFuncSetAttribute(qmm_small)");
+  if (rc) return rc;
+  // Two CTAs share an SM when their shared memory fits: ask for the largest
+  // shared-memory carveout (the default may leave room for one).
+  static const bool carveout_set = [] {
+    return cudaFuncSetAttribute(reinterpret_cast<const void*>(qmm_small_kernel<MT>),
+                                cudaFuncAttributePreferredSharedMemoryCarveout,
+                                cudaSharedmemCarveoutMaxShared) == cudaSuccess;
+  }();
+  (void)carveout_set;
+  CUtensorMap tm_x, tm_c;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(a.w_cols), static_cast<uint64_t>(a.m)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(a.w_cols) * 2};
+    const uint32_t box[2] = {64, static_cast<uint32_t>(C::MPAD)};
+    rc = encode_tmap(&tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.x, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  {
+    // Codes as u32 [w_rows, w_cols / 8]: 16 words (one 128-k chunk) x 128 rows.
+    const uint64_t dims[2] = {static_cast<uint64_t>(a.w_cols / 8), static_cast<uint64_t>(a.w_rows)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(a.w_cols / 2)};
+    const uint32_t box[2] = {kSmallChunk / 8, static_cast<uint32_t>(kSmallRows)};
+    rc = encode_tmap(&tm_c, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, a.codes, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc) return rc;
+  }
+  SmallParams p{};
+  p.codes = static_cast<const uint32_t*>(a.codes);
+  p.scales = static_cast<const uint16_t*>(a.scales);
+  p.biases = static_cast<const uint16_t*>(a.biases);
+  p.bias = static_cast<const uint16_t*>(a.bias);
+  p.y = static_cast<uint16_t*>(a.y);
+  p.m = static_cast<int>(a.m);
+  p.n = static_cast<int>(a.w_rows);
+  p.k = static_cast<int>(a.w_cols);
+  p.group = a.group_size;
+  p.cs = pl.small_cs;
+  p.status = status;
+  const int64_t blocks = (a.w_rows + kSmallRows - 1) / kSmallRows;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks * pl.small_cs), 1, 1);
+  cfg.blockDim = dim3(kSmallThreads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(C::smem(pl.small_cs));
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(pl.small_cs);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pl.small_cs > 1 ? 1 : 0;
+  return check_cuda(cudaLaunchKernelEx(&cfg, qmm_small_kernel<MT>, tm_x, tm_c, p),
+                    "quantized_matmul (small) launch");
+}
+
+int launch_small(const Args& a, const Plan& pl, cudaStream_t stream, int* status) {
+  switch ((a.m + 7) / 8) {
+    case 1: return launch_small_mt<1>(a, pl, stream, status);
+    case 2: return launch_small_mt<2>(a, pl, stream, status);
+    case 3: return launch_small_mt<3>(a, pl, stream, status);
+    default: return launch_small_mt<4>(a, pl, stream, status);
+  }
+}
+
 int validate(const Args& a) {
   if (a.bits != 4 && a.bits != 8) return fail(TQ_ERR_UNSUPPORTED, "bits must be 4 or 8, got %d", a.bits);
   if (a.group_size != 32 && a.group_size != 64 && a.group_size != 128)
@@ -1168,6 +1270,7 @@ int run(const Args& a, void* stream) {
   int* status = device_status_ptr(&rc);
   if (!status) return rc;
   cudaStream_t s = as_stream(stream);
+  if (pl.small) return launch_small(a, pl, s, status);
   if (a.bits == 4)
     return a.transpose ? launch_bn<4, true>(a, pl, s, status) : launch_bn<4, false>(a, pl, s, status);
   return a.transpose ? launch_bn<8, true>(a, pl, s, status) : launch_bn<8, false>(a, pl, s, status);

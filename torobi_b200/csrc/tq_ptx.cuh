@@ -465,6 +465,34 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t cbar) {
       : "memory");
 }
 
+// ------------------------------------------------------- warp-level MMA ---
+//
+// For the small-token quantized GEMM, whose weight operand is dequantized in
+// registers and never staged in shared memory.
+
+// D (16 x 8, f32) += A (16 x 16, bf16, row) * B (16 x 8, bf16, col).
+// Lane l holds A rows l/4 and l/4 + 8, columns 2(l%4) + {0,1} (registers 0, 1)
+// and + 8 (registers 2, 3); B rows 2(l%4) + {0,1} and + 8, column l/4; D rows
+// l/4 and l/4 + 8, columns 2(l%4) + {0,1}.
+__device__ __forceinline__ void mma_16816_bf16(float (&d)[4], uint32_t a0, uint32_t a1,
+                                               uint32_t a2, uint32_t a3, uint32_t b0,
+                                               uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+      "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// 16-byte global load that bypasses L1 (data read once).
+__device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
 // ------------------------------------------------------- bf16x2 arithmetic --
 
 // Round-to-nearest-even a*b + c on packed bf16 pairs (single rounding).
