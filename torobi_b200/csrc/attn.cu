@@ -78,14 +78,16 @@ struct FwdCfg {
   static constexpr int SLABS = D / 64;            // 128-byte swizzle atoms along dim
   static constexpr int SLAB_BYTES = kTile * 128;  // 128 rows x 64 bf16
   static constexpr int TILE_BYTES = SLABS * SLAB_BYTES;
-  static constexpr int STAGES = D == 128 ? 2 : 4;
+  // Key tiles are needed a step before value tiles, so their ring is deeper.
+  static constexpr int KST = D == 128 ? 3 : 4;
+  static constexpr int VST = D == 128 ? 2 : 4;
   static constexpr int Q_OFF = 0;  // two query tiles
   static constexpr int K_OFF = 2 * TILE_BYTES;
-  static constexpr int V_OFF = K_OFF + STAGES * TILE_BYTES;
-  static constexpr int BAR_OFF = V_OFF + STAGES * TILE_BYTES;
-  // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2],
+  static constexpr int V_OFF = K_OFF + KST * TILE_BYTES;
+  static constexpr int BAR_OFF = V_OFF + VST * TILE_BYTES;
+  // q_full, k_full[KST], k_empty[KST], v_full[VST], v_empty[VST], s_full[2],
   // p_ready[2], o_done[2]; then the TMEM slot
-  static constexpr int NBAR = 1 + 4 * STAGES + 6;
+  static constexpr int NBAR = 1 + 2 * KST + 2 * VST + 6;
   static constexpr int SMEM = 1024 + BAR_OFF + 8 * (NBAR + 1);
   static constexpr int S_COL = 0;    // S_w (and P_w) at 128 w
   static constexpr int O_COL = 256;  // O_w at 256 + D w
@@ -107,7 +109,8 @@ __global__ void __launch_bounds__(384, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
   using C = FwdCfg<D>;
-  constexpr int ST = C::STAGES;
+  constexpr int KST = C::KST;
+  constexpr int VST = C::VST;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -118,16 +121,17 @@ __global__ void __launch_bounds__(384, 1)
   const uint32_t bars = base + C::BAR_OFF;
   const uint32_t q_full = bars;
   auto k_full = [&](int s) { return bars + 8u * (1 + s); };
-  auto k_empty = [&](int s) { return bars + 8u * (1 + ST + s); };
-  auto v_full = [&](int s) { return bars + 8u * (1 + 2 * ST + s); };
-  auto v_empty = [&](int s) { return bars + 8u * (1 + 3 * ST + s); };
+  auto k_empty = [&](int s) { return bars + 8u * (1 + KST + s); };
+  auto v_full = [&](int s) { return bars + 8u * (1 + 2 * KST + s); };
+  auto v_empty = [&](int s) { return bars + 8u * (1 + 2 * KST + VST + s); };
+  constexpr int X = 1 + 2 * KST + 2 * VST;
   // Per query tile w, each completing once per key tile j (phase j):
   // s_full (S_w(j) landed), p_ready (P_w(j) written, O_w rescaled), o_done
   // (PV_w(j) finished).  S_w(j+1) is only issued after p_ready's phase j, so
   // no waiter is ever two phases behind.
-  auto s_full = [&](int w) { return bars + 8u * (1 + 4 * ST + w); };
-  auto p_ready = [&](int w) { return bars + 8u * (3 + 4 * ST + w); };
-  auto o_done = [&](int w) { return bars + 8u * (5 + 4 * ST + w); };
+  auto s_full = [&](int w) { return bars + 8u * (X + w); };
+  auto p_ready = [&](int w) { return bars + 8u * (X + 2 + w); };
+  auto o_done = [&](int w) { return bars + 8u * (X + 4 + w); };
   const uint32_t tmem_slot = bars + 8u * C::NBAR;
   volatile uint32_t* tmem_slot_ptr =
       reinterpret_cast<volatile uint32_t*>(gbase + (tmem_slot - base));
@@ -150,9 +154,11 @@ __global__ void __launch_bounds__(384, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < ST; ++s) {
+    for (int s = 0; s < KST; ++s) {
       mbar_init(k_full(s), 1);
       mbar_init(k_empty(s), 1);
+    }
+    for (int s = 0; s < VST; ++s) {
       mbar_init(v_full(s), 1);
       mbar_init(v_empty(s), 1);
     }
@@ -183,15 +189,22 @@ __global__ void __launch_bounds__(384, 1)
         for (int sl = 0; sl < C::SLABS; ++sl)
           tma_load_4d(q_s(w) + sl * C::SLAB_BYTES, &tm_q, q_full, sl * 64, h, (t0 + w) * kTile, b);
       int nk = 0, nv = 0;  // tiles issued
-      for (int j = 0; j < n_kv; ++j) {
-        const int s = j % ST;
-        const uint32_t ph = (j / ST) & 1;
-        if (!mbar_wait(k_empty(s), ph ^ 1, p.status)) break;
+      // Key tile j + 1 is issued ahead of value tile j (the MMA wants K_{j+1}
+      // for the next scores before it wants V_j).
+      auto load_k = [&](int j) -> bool {
+        const int s = j % KST;
+        if (!mbar_wait(k_empty(s), ((j / KST) & 1) ^ 1, p.status)) return false;
         mbar_arrive_expect_tx(k_full(s), C::TILE_BYTES);
         for (int sl = 0; sl < C::SLABS; ++sl)
           tma_load_4d(k_s(s) + sl * C::SLAB_BYTES, &tm_k, k_full(s), sl * 64, hk, j * kTile, b);
         ++nk;
-        if (!mbar_wait(v_empty(s), ph ^ 1, p.status)) break;
+        return true;
+      };
+      bool ok = n_kv > 0 ? load_k(0) : true;
+      for (int j = 0; j < n_kv && ok; ++j) {
+        if (j + 1 < n_kv && !load_k(j + 1)) break;
+        const int s = j % VST;
+        if (!mbar_wait(v_empty(s), ((j / VST) & 1) ^ 1, p.status)) break;
         mbar_arrive_expect_tx(v_full(s), C::TILE_BYTES);
         for (int sl = 0; sl < C::SLABS; ++sl)
           tma_load_4d(v_s(s) + sl * C::SLAB_BYTES, &tm_v, v_full(s), sl * 64, hk, j * kTile, b);
@@ -199,10 +212,10 @@ __global__ void __launch_bounds__(384, 1)
       }
       // Never leave a copy in flight.
       mbar_wait(q_full, 0, p.status);
-      for (int j = nk - ST < 0 ? 0 : nk - ST; j < nk; ++j)
-        mbar_wait(k_full(j % ST), (j / ST) & 1, p.status);
-      for (int j = nv - ST < 0 ? 0 : nv - ST; j < nv; ++j)
-        mbar_wait(v_full(j % ST), (j / ST) & 1, p.status);
+      for (int j = nk - KST < 0 ? 0 : nk - KST; j < nk; ++j)
+        mbar_wait(k_full(j % KST), (j / KST) & 1, p.status);
+      for (int j = nv - VST < 0 ? 0 : nv - VST; j < nv; ++j)
+        mbar_wait(v_full(j % VST), (j / VST) & 1, p.status);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------- MMA
@@ -212,7 +225,7 @@ __global__ void __launch_bounds__(384, 1)
       bool ok = mbar_wait(q_full, 0, p.status);
       // S_w(j) = Q_w K_j^T into S_w.
       auto issue_s = [&](int w, int j) {
-        const int s = j % ST;
+        const int s = j % KST;
         const uint32_t d = tmem + C::S_COL + w * kTile;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -224,7 +237,7 @@ __global__ void __launch_bounds__(384, 1)
       };
       // O_w += P_w(j) V_j, P_w from the first 64 columns of S_w.
       auto issue_pv = [&](int w, int j) {
-        const int s = j % ST;
+        const int s = j % VST;
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)
           umma_bf16_ts(tmem + C::O_COL + w * D, tmem + C::S_COL + w * kTile + kk * 8,
@@ -241,13 +254,13 @@ __global__ void __launch_bounds__(384, 1)
         umma_commit(k_empty(0));
       }
       for (int j = 0; j < n_kv && ok; ++j) {
-        const int s = j % ST;
+        const int s = j % VST;
         const bool next = j + 1 < n_kv;
         if (next) {
-          ok = mbar_wait(k_full((j + 1) % ST), ((j + 1) / ST) & 1, p.status);
+          ok = mbar_wait(k_full((j + 1) % KST), ((j + 1) / KST) & 1, p.status);
           if (!ok) break;
         }
-        ok = mbar_wait(v_full(s), (j / ST) & 1, p.status);
+        ok = mbar_wait(v_full(s), (j / VST) & 1, p.status);
         if (!ok) break;
         for (int w = 0; w < 2 && ok; ++w) {
           if (j >= nkv_of(w)) continue;
@@ -259,7 +272,7 @@ __global__ void __launch_bounds__(384, 1)
         }
         if (!ok) break;
         umma_commit(v_empty(s));
-        if (next) umma_commit(k_empty((j + 1) % ST));
+        if (next) umma_commit(k_empty((j + 1) % KST));
       }
       // Nothing may outlive the CTA's TMEM: wait for each tile's last PV.
       for (int w = 0; w < 2; ++w)
@@ -432,13 +445,15 @@ __global__ void __launch_bounds__(384, 1)
 //   prep   per query row: lse2 = lse * log2(e) and delta = sum_d dO * O (f32),
 //          each (sequence, head)'s rows padded to whole 128-row tiles (padding
 //          rows: lse2 = +inf, so their probabilities are 0, and delta = 0);
-//   dq     one CTA per (128-query tile, head, sequence), key tiles of 64:
+//   dq     one CTA per (128-query tile, head, sequence), key tiles of 64
+//          (two compute warpgroups, each half of every tile's columns):
 //            S = Q K_j^T, dP = dO V_j^T (tensor memory, double-buffered),
 //            dS = P * (dP - delta) with P = exp2(S c - lse2)  (compute warps),
 //            dQ += dS K_j  (dS written back to tensor memory, A from TMEM);
 //   dkv    one CTA per (128-key tile, key/value head, sequence), looping over
 //          the query heads that share the key/value head and their 64-row
-//          query tiles:
+//          query tiles (two compute warpgroups, each half of every tile's
+//          columns):
 //            S^T = K Q_i^T, dP^T = V dO_i^T, P^T and dS^T (compute warps, into
 //            shared memory as K-major operands), dV += P^T dO_i, dK += dS^T Q_i.
 // dQ and dK are scaled by the softmax scale once at the end.  As in the
@@ -517,7 +532,7 @@ struct DqCfg {
   static constexpr int QTILE = SLABS * QSLAB;
   static constexpr int KSLAB = kHalf * 128;  // 64 rows x 64 bf16
   static constexpr int KTILE = SLABS * KSLAB;
-  static constexpr int KST = D == 128 ? 3 : 4;
+  static constexpr int KST = D == 128 ? 5 : 8;
   static constexpr int VST = KST;
   static constexpr int Q_OFF = 0;
   static constexpr int DO_OFF = QTILE;
@@ -540,7 +555,7 @@ struct DqCfg {
 };
 
 template <int D>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(384, 1)
     attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_do,
                        const __grid_constant__ CUtensorMap tm_k,
@@ -597,8 +612,8 @@ __global__ void __launch_bounds__(256, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(s_full(i), 1);
-      mbar_init(s_free(i), 4);
-      mbar_init(ds_ready(i), 4);
+      mbar_init(s_free(i), 8);
+      mbar_init(ds_ready(i), 8);
     }
     mbar_init(dq_full, 1);
     fence_mbar_init();
@@ -702,6 +717,10 @@ __global__ void __launch_bounds__(256, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------ compute warps
+    // Two warpgroups on the same 128 rows: warps 4-7 take key columns 0-31
+    // of each 64-key tile, warps 8-11 columns 32-63 (the gradient is
+    // elementwise given the row's lse and delta); likewise halves of dQ.
+    const int half = (warp - 4) >> 2;
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
     const int qpos = q0 + row;
@@ -715,34 +734,31 @@ __global__ void __launch_bounds__(256, 1)
       ok = mbar_wait(s_full(j & 1), (j >> 1) & 1, p.status);
       if (!ok) break;
       tc_fence_after();
-      uint32_t sv[kHalf], dv[kHalf];
-      tmem_ld_32x32b_x32(lrow + C::S_COL + (j & 1) * kHalf, *reinterpret_cast<uint32_t(*)[32]>(sv));
-      tmem_ld_32x32b_x32(lrow + C::S_COL + (j & 1) * kHalf + 32,
-                         *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-      tmem_ld_32x32b_x32(lrow + C::DP_COL + (j & 1) * kHalf, *reinterpret_cast<uint32_t(*)[32]>(dv));
-      tmem_ld_32x32b_x32(lrow + C::DP_COL + (j & 1) * kHalf + 32,
-                         *reinterpret_cast<uint32_t(*)[32]>(dv + 32));
+      uint32_t sv[32], dv[32];
+      tmem_ld_32x32b_x32(lrow + C::S_COL + (j & 1) * kHalf + half * 32, sv);
+      tmem_ld_32x32b_x32(lrow + C::DP_COL + (j & 1) * kHalf + half * 32, dv);
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(s_free(j & 1));
-      const int kv0 = j * kHalf;
-      int lim = kHalf - 1;  // last column of this tile that counts
-      if ((sh.causal && kv0 + kHalf - 1 > q0) || kv0 + kHalf > sh.seq) {
+      const int kv0 = j * kHalf + half * 32;
+      int lim = 31;  // last column of this half tile that counts
+      if ((sh.causal && kv0 + 31 > q0) || kv0 + 32 > sh.seq) {
         lim = sh.seq - 1 - kv0;
         if (sh.causal && qpos - kv0 < lim) lim = qpos - kv0;
       }
-      uint32_t pk[kHalf / 2];
+      uint32_t pk[16];
 #pragma unroll
-      for (int i = 0; i < kHalf; i += 2) {
+      for (int i = 0; i < 32; i += 2) {
         float p0 = ex2_approx(fmaf(__uint_as_float(sv[i]), c, -lse2));
-        float p1 = ex2_approx(fmaf(__uint_as_float(sv[i + 1]), c, -lse2));
+        float p1 = (i & 2) ? exp2_poly(fmaf(__uint_as_float(sv[i + 1]), c, -lse2))
+                           : ex2_approx(fmaf(__uint_as_float(sv[i + 1]), c, -lse2));
         if (i > lim) p0 = 0.0f;
         if (i + 1 > lim) p1 = 0.0f;
         pk[i / 2] = pack_bf16x2_f32(p0 * (__uint_as_float(dv[i]) - dl),
                                     p1 * (__uint_as_float(dv[i + 1]) - dl));
       }
-      tmem_st_32x32b_x32(lrow + C::DS_COL + (j & 1) * 32, pk);
+      tmem_st_32x32b_x16(lrow + C::DS_COL + (j & 1) * 32 + half * 16, pk);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
@@ -754,7 +770,7 @@ __global__ void __launch_bounds__(256, 1)
       const bool valid = qpos < sh.seq;
       uint16_t* orow = p.dq + ((static_cast<size_t>(b) * sh.seq + qpos) * sh.heads + h) * D;
 #pragma unroll
-      for (int c4 = 0; c4 < D / 32; ++c4) {
+      for (int c4 = half * (D / 64); c4 < (half + 1) * (D / 64); ++c4) {
         uint32_t o[32];
         tmem_ld_32x32b_x32(lrow + C::DQ_COL + c4 * 32, o);
         tmem_ld_wait();
@@ -790,7 +806,7 @@ struct DkvCfg {
   static constexpr int QSLAB = kHalf * 128;  // Q_i, dO_i: 64 rows x 64 bf16
   static constexpr int QTILE = SLABS * QSLAB;
   static constexpr int PTILE = kTile * 128;  // P^T or dS^T: 128 key rows x 64 queries bf16
-  static constexpr int QST = D == 128 ? 2 : 3;
+  static constexpr int QST = D == 128 ? 3 : 6;
   static constexpr int STAT_BYTES = 2 * kHalf * 4;  // lse2 and delta of one query tile
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = KTILE;
@@ -815,7 +831,7 @@ struct DkvCfg {
 };
 
 template <int D>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(384, 1)
     attn_bwd_dkv_kernel(const __grid_constant__ CUtensorMap tm_q,
                         const __grid_constant__ CUtensorMap tm_do,
                         const __grid_constant__ CUtensorMap tm_k,
@@ -864,12 +880,12 @@ __global__ void __launch_bounds__(256, 1)
     mbar_init(kv_full, 1);
     for (int s = 0; s < QST; ++s) {
       mbar_init(q_full(s), 1);
-      mbar_init(q_empty(s), 1 + 4);  // the MMAs' commit and the compute warps' stat reads
+      mbar_init(q_empty(s), 1 + 8);  // the MMAs' commit and the compute warps' stat reads
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(s_full(i), 1);
-      mbar_init(s_free(i), 4);
-      mbar_init(pds_ready(i), 4);
+      mbar_init(s_free(i), 8);
+      mbar_init(pds_ready(i), 8);
     }
     mbar_init(acc_full, 1);
     fence_mbar_init();
@@ -971,6 +987,10 @@ __global__ void __launch_bounds__(256, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------ compute warps
+    // Two warpgroups on the same 128 key rows: warps 4-7 take query columns
+    // 0-31 of each 64-query tile, warps 8-11 columns 32-63; likewise halves
+    // of the dV and dK rows at the end.
+    const int half = (warp - 4) >> 2;
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
     const int kvpos = kv0 + row;
@@ -979,17 +999,13 @@ __global__ void __launch_bounds__(256, 1)
     bool ok = true;
     for (int t = 0; t < T; ++t) {
       const int s = t % QST;
-      const int qq0 = (i0 + t % nq) * kHalf;
+      const int qq0 = (i0 + t % nq) * kHalf + half * 32;
       ok = mbar_wait(s_full(t & 1), (t >> 1) & 1, p.status);
       if (!ok) break;
       tc_fence_after();
-      uint32_t sv[kHalf], dv[kHalf];
-      tmem_ld_32x32b_x32(lrow + C::S_COL + (t & 1) * kHalf, *reinterpret_cast<uint32_t(*)[32]>(sv));
-      tmem_ld_32x32b_x32(lrow + C::S_COL + (t & 1) * kHalf + 32,
-                         *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-      tmem_ld_32x32b_x32(lrow + C::DP_COL + (t & 1) * kHalf, *reinterpret_cast<uint32_t(*)[32]>(dv));
-      tmem_ld_32x32b_x32(lrow + C::DP_COL + (t & 1) * kHalf + 32,
-                         *reinterpret_cast<uint32_t(*)[32]>(dv + 32));
+      uint32_t sv[32], dv[32];
+      tmem_ld_32x32b_x32(lrow + C::S_COL + (t & 1) * kHalf + half * 32, sv);
+      tmem_ld_32x32b_x32(lrow + C::DP_COL + (t & 1) * kHalf + half * 32, dv);
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
@@ -997,14 +1013,14 @@ __global__ void __launch_bounds__(256, 1)
       // The query tile's lse2 and delta (landed with its Q and dO).
       ok = mbar_wait(q_full(s), (t / QST) & 1, p.status);
       if (!ok) break;
-      const float* st = reinterpret_cast<const float*>(gbase + (stat_s(s) - base));
+      const float* st = reinterpret_cast<const float*>(gbase + (stat_s(s) - base)) + half * 32;
       // A key row sees query q only if q >= kvpos (causal); rows past seq
       // carry lse2 = +inf, so their probabilities are 0 already.
       int first = 0;
       if (sh.causal && qq0 < kvpos) first = kvpos - qq0;
-      uint32_t pk[kHalf / 2], dk[kHalf / 2];
+      uint32_t pk[16], dk[16];
 #pragma unroll
-      for (int i = 0; i < kHalf; i += 4) {
+      for (int i = 0; i < 32; i += 4) {
         const float4 l4 = *reinterpret_cast<const float4*>(st + i);
         const float4 d4 = *reinterpret_cast<const float4*>(st + kHalf + i);
         const float la[4] = {l4.x, l4.y, l4.z, l4.w};
@@ -1012,7 +1028,8 @@ __global__ void __launch_bounds__(256, 1)
         float pv[4], dsv[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          float pe = ex2_approx(fmaf(__uint_as_float(sv[i + e]), c, -la[e]));
+          const float x = fmaf(__uint_as_float(sv[i + e]), c, -la[e]);
+          float pe = e == 3 ? exp2_poly(x) : ex2_approx(x);
           if (i + e < first) pe = 0.0f;
           pv[e] = pe;
           dsv[e] = pe * (__uint_as_float(dv[i + e]) - da[e]);
@@ -1025,14 +1042,15 @@ __global__ void __launch_bounds__(256, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(q_empty(s));
       // Row `row` of the K-major operand: 64 bf16 = eight 16-byte chunks,
-      // chunk ch stored at ch ^ (row & 7) (the 128-byte swizzle).
+      // chunk ch stored at ch ^ (row & 7) (the 128-byte swizzle); this half
+      // writes chunks 4 half .. 4 half + 3.
       const uint32_t prow = p_s(t & 1) + row * 128;
       const uint32_t drow = ds_s(t & 1) + row * 128;
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        const uint32_t off = static_cast<uint32_t>((ch ^ (row & 7)) * 16);
-        sts128(prow + off, pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
-        sts128(drow + off, dk[4 * ch], dk[4 * ch + 1], dk[4 * ch + 2], dk[4 * ch + 3]);
+      for (int q4 = 0; q4 < 4; ++q4) {
+        const uint32_t off = static_cast<uint32_t>(((4 * half + q4) ^ (row & 7)) * 16);
+        sts128(prow + off, pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+        sts128(drow + off, dk[4 * q4], dk[4 * q4 + 1], dk[4 * q4 + 2], dk[4 * q4 + 3]);
       }
       fence_proxy_async_smem();
       __syncwarp();
@@ -1049,7 +1067,7 @@ __global__ void __launch_bounds__(256, 1)
         const float f = which == 0 ? 1.0f : p.scale;
         uint16_t* orow = (which == 0 ? p.dv : p.dk) + roff;
 #pragma unroll
-        for (int c4 = 0; c4 < D / 32; ++c4) {
+        for (int c4 = half * (D / 64); c4 < (half + 1) * (D / 64); ++c4) {
           uint32_t o[32];
           tmem_ld_32x32b_x32(lrow + col + c4 * 32, o);
           tmem_ld_wait();
@@ -1193,11 +1211,11 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* out, con
   p.dv = static_cast<uint16_t*>(dv);
   p.status = status;
   const unsigned grid_q = static_cast<unsigned>(sh.batch) * sh.heads * sh.n_tiles;
-  attn_bwd_dq_kernel<D><<<grid_q, 256, Q::SMEM, stream>>>(q128, do128, k64, v64, p);
+  attn_bwd_dq_kernel<D><<<grid_q, 384, Q::SMEM, stream>>>(q128, do128, k64, v64, p);
   rc = check_cuda(cudaGetLastError(), "attention backward dq launch");
   if (rc) return rc;
   const unsigned grid_kv = static_cast<unsigned>(sh.batch) * sh.kv_heads * sh.n_tiles;
-  attn_bwd_dkv_kernel<D><<<grid_kv, 256, KV::SMEM, stream>>>(q64, do64, k128, v128, p);
+  attn_bwd_dkv_kernel<D><<<grid_kv, 384, KV::SMEM, stream>>>(q64, do64, k128, v128, p);
   return check_cuda(cudaGetLastError(), "attention backward dkv launch");
 }
 
