@@ -806,15 +806,26 @@ Plan make_plan(const Args& a, bool allow_split) {
     const bool ts = a.transpose && !ts_off;
     const int top = ts ? 192 : 256;
     const int cands[2] = {top, 128};
+    // Among the token tiles that keep at least three quarters of the pairs
+    // busy, the one with the least estimated time: waves x tile cost, a
+    // 128-token tile costing 1/0.7 of its tokens' share of a 256-token one
+    // (its weight tile is dequantized for half as many tokens).  At 1024
+    // tokens x 4096 outputs this picks one wave of 256-token tiles (64 of
+    // 74 pairs) over two waves of 128-token ones.
+    double best = 0.0;
     for (int cand : cands) {
       if ((forced == 256 || forced == 192 || forced == 128) &&
           (forced == 128) != (cand == 128))
         continue;
-      if (a.m >= cand / 2 && ((a.m + cand - 1) / cand) * pair_tiles_n >= pairs) {
+      const int64_t tiles = ((a.m + cand - 1) / cand) * pair_tiles_n;
+      if (a.m < cand / 2 || 4 * tiles < 3 * pairs) continue;
+      const int64_t waves = (tiles + pairs - 1) / pairs;
+      const double cost = static_cast<double>(waves) * cand / (cand == 128 ? 0.7 : 1.0);
+      if (!pl.pair || cost < best) {
         pl.pair = true;
         pl.ts = ts;
         pl.bn = cand;
-        break;
+        best = cost;
       }
     }
   }
