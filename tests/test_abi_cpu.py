@@ -101,3 +101,37 @@ def test_ops_refuse_cpu_tensors():
 
     with pytest.raises(ValueError, match="CUDA"):
         glue.add_rms_norm(w, w, w[0], 1e-6)
+
+
+def test_attention_argument_errors_need_no_gpu():
+    import torobi_b200 as tq
+    from torobi_b200._lib import TQ_ERR_INVALID, TQ_ERR_MISALIGNED, TQ_ERR_UNSUPPORTED
+
+    L = tq.lib()
+    p = 1 << 20  # 16-byte aligned stand-in address; nothing is dereferenced
+    args = lambda heads, kv, dim, scale, out: (p, p, p, 2, 128, heads, kv, dim, scale, 1, out, p, None)
+    assert L.tq_attention_fwd(*args(32, 12, 128, 0.1, p)) == TQ_ERR_INVALID
+    assert b"multiple of kv_heads" in L.tq_last_error()
+    assert L.tq_attention_fwd(*args(32, 8, 96, 0.1, p)) == TQ_ERR_UNSUPPORTED
+    assert b"head dim" in L.tq_last_error()
+    assert L.tq_attention_fwd(*args(32, 8, 128, 0.0, p)) == TQ_ERR_INVALID
+    assert b"scale" in L.tq_last_error()
+    assert L.tq_attention_fwd(*args(32, 8, 128, float("nan"), p)) == TQ_ERR_INVALID
+    assert L.tq_attention_fwd(*args(32, 8, 128, 0.1, p + 8)) == TQ_ERR_MISALIGNED
+    assert L.tq_attention_fwd(*args(32, 8, 128, 0.1, 0)) == TQ_ERR_INVALID
+    assert b"null" in L.tq_last_error()
+    # Empty batches are valid and touch nothing.
+    assert L.tq_attention_fwd(0, 0, 0, 0, 128, 32, 8, 128, 0.1, 1, 0, 0, None) == 0
+
+    need = ctypes.c_size_t(0)
+    assert L.tq_attention_bwd_workspace_bytes(2, 129, 4, ctypes.byref(need)) == 0
+    assert need.value == 2 * 2 * 4 * 256 * 4  # lse2 and delta, rows padded to 128-row tiles
+    assert L.tq_attention_bwd_workspace_bytes(2, 129, 0, ctypes.byref(need)) == TQ_ERR_INVALID
+
+    def bwd(ws_bytes, ws=p):
+        return L.tq_attention_bwd(p, p, p, p, p, p, 2, 129, 4, 2, 64, 0.125, 1, p, p, p, ws,
+                                  ws_bytes, None)
+
+    assert bwd(need.value - 4) == TQ_ERR_INVALID and b"workspace" in L.tq_last_error()
+    assert bwd(need.value, ws=p + 16) == TQ_ERR_MISALIGNED and b"256" in L.tq_last_error()
+    assert bwd(need.value, ws=0) == TQ_ERR_INVALID and b"null" in L.tq_last_error()
