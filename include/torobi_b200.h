@@ -182,6 +182,24 @@ int tq_qlora_matmul_ws(const void* x, const void* codes, const void* scales, con
                        size_t workspace_bytes, void* stream);
 
 /*
+ * tq_qlora_matmul_ws that adds its result into y instead of storing it:
+ *   y = RNE(RNE(result) + y)
+ * result being what tq_qlora_matmul_ws would write (bias and LoRA included),
+ * so a sum of several GEMMs built by calling this in turn equals the one a
+ * caller gets by adding their bf16 outputs one after another.  Used for the
+ * input gradient of linears that read one x (q/k/v, gate/up): MLX's VJP sums
+ * their cotangents for x (engine/src/executor.rs:163-191); this sums them in
+ * the GEMM's epilogue with no separate add.  The 4-bit small-token forward
+ * kernel is never used by this entry point.
+ */
+int tq_qlora_matmul_accumulate(const void* x, const void* codes, const void* scales,
+                               const void* biases, int64_t m, int64_t w_rows, int64_t w_cols,
+                               int transpose, int group_size, int bits, const void* bias,
+                               const void* lora_up, const void* lora_down, int64_t ld_down,
+                               int64_t rank, void* y, void* workspace, size_t workspace_bytes,
+                               void* stream);
+
+/*
  * tq_quantized_matmul with no workspace argument and no allocation: the
  * split-K partials live in a fixed 8 MiB array inside the library
  * (TQ_NOALLOC_SCRATCH_BYTES; every GPU that loads the library holds it until

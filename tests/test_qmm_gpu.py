@@ -311,3 +311,77 @@ def test_tensor_memory_weight_tile_variant(cuda):
     assert out.returncode == 0, out.stderr[-2000:]
     err = float(out.stdout.strip().splitlines()[-1])
     assert err <= TOL, f"max rel err {err:.3e}"
+
+
+# tq_qlora_matmul_accumulate: y = RNE(RNE(result) + y) through every epilogue
+# -- CTA pairs (TMA reduce-add), the single-CTA kernel's TMA reduce-add and
+# direct stores (y not 16-byte aligned), and split-K's reduce kernel -- bit
+# for bit what a separate bf16 add of the plain result gives.
+ACC_CASES = [
+    # (m, w_rows, w_cols, transpose, lora_rank, bias, y_misaligned)
+    (2048, 1024, 4096, False, 16, False, False),   # pairs, dX with LoRA (k/v-like)
+    (1000, 2304, 2560, True, 8, True, False),      # pairs, forward, bias + LoRA
+    (257, 128, 1024, True, 0, False, False),       # single CTA, TMA epilogue
+    (257, 392, 1024, False, 16, False, True),      # single CTA, direct stores
+    (16, 4096, 4096, False, 0, False, False),      # split-K (workspace), reduce kernel
+    (3, 256, 8192, True, 0, True, False),          # would be the small-token kernel
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", ACC_CASES,
+                         ids=lambda c: "m{}_n{}_k{}_t{}_r{}_b{}_u{}".format(*map(int, c)))
+def test_accumulate_equals_a_separate_add(cuda, oracle, case):
+    import torch
+    import torobi_b200 as tq
+
+    m, n, k, transpose, rank, with_bias, misaligned = case
+    torch.manual_seed(7)
+    w = (torch.randn(n, k, device=cuda) * 0.02).bfloat16()
+    c, s, b = tq.quantize(w, 64, 4)
+    k_in, n_out = (k, n) if transpose else (n, k)
+    x = torch.randn(m, k_in, device=cuda).bfloat16()
+    kw = {}
+    if rank:
+        kw["lora_up"] = (torch.randn(*((n, rank) if transpose else (rank, k)), device=cuda)
+                         * 0.05).bfloat16()
+        kw["lora_down"] = torch.randn(m, rank, device=cuda).bfloat16()
+    if with_bias:
+        kw["bias"] = torch.randn(n_out, device=cuda).bfloat16()
+    y0 = torch.randn(m, n_out, device=cuda).bfloat16()
+    want = y0.clone().add_(tq.qlora_matmul(x, c, s, b, transpose, 64, 4, **kw))
+    if misaligned:
+        buf = torch.empty(m * n_out + 1, dtype=torch.bfloat16, device=cuda)
+        acc = buf[1:].view(m, n_out)
+        assert acc.data_ptr() % 16 != 0
+    else:
+        acc = torch.empty_like(y0)
+    acc.copy_(y0)
+    got = tq.qlora_matmul(x, c, s, b, transpose, 64, 4, accumulate=acc, **kw)
+    assert got.data_ptr() == acc.data_ptr()
+    torch.cuda.synchronize()
+    assert torch.equal(got, want), (got.float() - want.float()).abs().max().item()
+    # And against the oracle: the quantized product (no LoRA or bias) plus y0.
+    if not rank and not with_bias:
+        from _util import host_bf16, host_u32
+
+        fn = oracle.qmm_fwd if transpose else oracle.qmm_dx
+        ref = fn(host_bf16(x), host_u32(c), host_bf16(s), host_bf16(b), 4, 64) + \
+            y0.float().cpu().numpy()
+        assert oracle.rel_err(got.float().cpu().numpy(), ref) <= TOL
+
+
+@pytest.mark.gpu
+def test_accumulate_argument_errors(cuda):
+    import torch
+    import torobi_b200 as tq
+
+    w = torch.zeros((128, 256), dtype=torch.bfloat16, device=cuda)
+    c, s, b = tq.quantize(w, 64, 4)
+    x = torch.zeros((4, 256), dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(ValueError, match="accumulate"):
+        tq.qlora_matmul(x, c, s, b, accumulate=torch.zeros((4, 64), dtype=torch.bfloat16,
+                                                           device=cuda))
+    with pytest.raises(ValueError, match="accumulate"):
+        tq.qlora_matmul(x, c, s, b, accumulate=torch.zeros((4, 128), dtype=torch.float32,
+                                                           device=cuda))

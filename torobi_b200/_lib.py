@@ -78,6 +78,8 @@ SIGNATURES = {
                                 ctypes.c_size_t, _vp], _i32),
     "tq_qlora_matmul_ws": ([_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _i32, _vp, _vp, _vp,
                             _i64, _i64, _vp, _vp, ctypes.c_size_t, _vp], _i32),
+    "tq_qlora_matmul_accumulate": ([_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _i32, _vp,
+                                    _vp, _vp, _i64, _i64, _vp, _vp, ctypes.c_size_t, _vp], _i32),
     "tq_quantized_matmul_noalloc": ([_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _i32, _vp,
                                      _vp], _i32),
     "tq_lora_down": ([_vp, _vp, _i64, _i64, _i64, _f32, _vp, _vp, _i64, _vp], _i32),

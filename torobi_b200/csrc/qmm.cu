@@ -109,6 +109,7 @@ struct Params {
   int k_steps_per_split;     // k-steps of every split but maybe the last
   float* ws;                 // splits > 1: f32 partials [splits, m, n_out]
   int tma_y;                 // the bf16 output goes out through TMA stores (tm_y)
+  int acc;                   // add into y: y = RNE(RNE(result) + y)
   int* status;
 };
 
@@ -624,7 +625,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) {
             const int og0 = out0 + q * 32;
-            if (og0 < p.n_out && m0 + c0 < p.m) tma_store_2d(&tm_y, sb, og0, m0 + c0);
+            if (og0 < p.n_out && m0 + c0 < p.m) {
+              if (p.acc)
+                tma_reduce_add_2d(&tm_y, sb, og0, m0 + c0);
+              else
+                tma_store_2d(&tm_y, sb, og0, m0 + c0);
+            }
             tma_store_commit();
           }
         } else if (ok && og < p.n_out) {
@@ -639,9 +645,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint16_t* yp = p.y + static_cast<size_t>(m0 + c0) * p.n_out + og;
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              if (j < mlim)
-                yp[static_cast<size_t>(j) * p.n_out] =
-                    __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[j]) + bias));
+              if (j < mlim) {
+                uint16_t* e = yp + static_cast<size_t>(j) * p.n_out;
+                __nv_bfloat16 r = __float2bfloat16_rn(__uint_as_float(v[j]) + bias);
+                if (p.acc)
+                  r = __float2bfloat16_rn(__bfloat162float(r) +
+                                          __uint_as_float(uint32_t(*e) << 16));
+                *e = __bfloat16_as_ushort(r);
+              }
             }
           }
         }
@@ -689,6 +700,7 @@ struct Args {
   void* ws = nullptr;        // split-K workspace (f32), or null: no split
   size_t ws_bytes = 0;
   int64_t ld_down = 0;       // row pitch of lora_down in elements (0: rank)
+  int acc = 0;               // add the result into y instead of storing it
 };
 
 // How a call is run: the token tile, whether the scale tiles ride in the TMA
@@ -737,7 +749,7 @@ bool small_ok(const Args& a) {
     const char* e = getenv("TQ_QMM_SMALL");
     return e && e[0] == '0';
   }();
-  return !off && a.transpose && a.bits == 4 && a.m >= 1 && a.m <= kSmallMaxM && a.rank == 0 &&
+  return !off && !a.acc && a.transpose && a.bits == 4 && a.m >= 1 && a.m <= kSmallMaxM && a.rank == 0 &&
          a.w_cols % kSmallChunk == 0 && a.w_rows % 16 == 0 && aligned(a.x, 16) &&
          aligned(a.y, 16);
 }
@@ -832,11 +844,12 @@ Plan make_plan(const Args& a, bool allow_split) {
   return pl;
 }
 
-// y[m, n] = bf16(sum over splits of ws[s, m, n] + bias[n]); 8 outputs a thread.
+// y[m, n] = bf16(sum over splits of ws[s, m, n] + bias[n]); 8 outputs a
+// thread.  acc: that value is then added to y's and rounded again.
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ ws,
                                                             int splits, int64_t m, int n,
                                                             const uint16_t* __restrict__ bias,
-                                                            uint16_t* __restrict__ y) {
+                                                            int acc_y, uint16_t* __restrict__ y) {
   const int64_t nv = m * n / 8;
   const int64_t plane = m * n;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -858,6 +871,16 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
       const int col = static_cast<int>(e % n);
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] += __uint_as_float(uint32_t(__ldg(bias + col + j)) << 16);
+    }
+    if (acc_y) {
+      const uint4 old = reinterpret_cast<const uint4*>(y)[v];
+      const uint32_t w[4] = {old.x, old.y, old.z, old.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[2 * j] = __bfloat162float(__float2bfloat16_rn(acc[2 * j])) + __uint_as_float(w[j] << 16);
+        acc[2 * j + 1] = __bfloat162float(__float2bfloat16_rn(acc[2 * j + 1])) +
+                         __uint_as_float(w[j] & 0xFFFF0000u);
+      }
     }
     uint4 o;
     o.x = pack_bf16x2_f32(acc[0], acc[1]);
@@ -973,6 +996,7 @@ Params make_params(const Args& a, const Plan& pl, int tile_rows, int bn, int* st
   p.k_steps_per_split = pl.k_steps_per_split;
   p.ws = static_cast<float*>(a.ws);
   p.tma_y = 0;
+  p.acc = a.acc;
   p.status = status;
   return p;
 }
@@ -1012,7 +1036,7 @@ int launch(const Args& a, const Plan& pl, cudaStream_t stream, int* status) {
   if (rgrid > sm_count() * 8) rgrid = sm_count() * 8;
   splitk_reduce_kernel<<<rgrid, 256, 0, stream>>>(
       static_cast<const float*>(a.ws), pl.splits, a.m, static_cast<int>(n_out),
-      static_cast<const uint16_t*>(a.bias), static_cast<uint16_t*>(a.y));
+      static_cast<const uint16_t*>(a.bias), a.acc, static_cast<uint16_t*>(a.y));
   return check_cuda(cudaGetLastError(), "split-K reduce launch");
 }
 
@@ -1344,6 +1368,21 @@ extern "C" int tq_qlora_matmul_ws(const void* x, const void* codes, const void* 
   tq::Args a{x, codes, scales, biases, bias, lora_up, lora_down, m, w_rows, w_cols,
              transpose, group_size, bits, static_cast<int>(rank), y, workspace, workspace_bytes};
   a.ld_down = ld_down;
+  return tq::run(a, stream);
+}
+
+extern "C" int tq_qlora_matmul_accumulate(const void* x, const void* codes, const void* scales,
+                                          const void* biases, int64_t m, int64_t w_rows,
+                                          int64_t w_cols, int transpose, int group_size,
+                                          int bits, const void* bias, const void* lora_up,
+                                          const void* lora_down, int64_t ld_down, int64_t rank,
+                                          void* y, void* workspace, size_t workspace_bytes,
+                                          void* stream) {
+  if (rank < 0 || rank > 16) return tq::fail(TQ_ERR_UNSUPPORTED, "LoRA rank must be 8 or 16");
+  tq::Args a{x, codes, scales, biases, bias, lora_up, lora_down, m, w_rows, w_cols,
+             transpose, group_size, bits, static_cast<int>(rank), y, workspace, workspace_bytes};
+  a.ld_down = ld_down;
+  a.acc = 1;
   return tq::run(a, stream);
 }
 

@@ -366,7 +366,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         // "all but the newest group have read" always covers this buffer's
         // previous store.
         if (lane == 0) {
-          if (og0 < p.n_out && m0 + c0 < p.m) tma_store_2d(&tm_y, sb, og0, m0 + c0);
+          if (og0 < p.n_out && m0 + c0 < p.m) {
+            if (p.acc)
+              tma_reduce_add_2d(&tm_y, sb, og0, m0 + c0);
+            else
+              tma_store_2d(&tm_y, sb, og0, m0 + c0);
+          }
           tma_store_commit();
         }
       }

@@ -333,12 +333,16 @@ def quantized_matmul(x: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor,
 def qlora_matmul(x: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
                  transpose: bool = True, group_size: int = 64, bits: int = 4,
                  bias: torch.Tensor | None = None, lora_up: torch.Tensor | None = None,
-                 lora_down: torch.Tensor | None = None) -> torch.Tensor:
+                 lora_down: torch.Tensor | None = None,
+                 accumulate: torch.Tensor | None = None) -> torch.Tensor:
     """quantized_matmul plus bias and the LoRA up-projection in one kernel.
 
     transpose: y = x W^T + bias + lora_down . lora_up^T   (lora_up = B [n, r])
     otherwise: y = x W + lora_down . lora_up               (lora_up = A [r, k])
     ``lora_down`` is the [m, r] bf16 down-projection already scaled by alpha/r.
+    ``accumulate`` (a contiguous bf16 tensor of y's shape): the result is added
+    into it in the GEMM's epilogue, ``accumulate = RNE(RNE(y) + accumulate)``
+    (what ``accumulate.add_(y)`` gives), and it is returned.
     """
     op = "qlora_matmul"
     x2, w_rows, w_cols, n_out = _gemm_operands(op, x, w_q, scales, biases, transpose,
@@ -370,7 +374,18 @@ def qlora_matmul(x: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, biase
             raise ValueError(f"[{op}] a bias is only defined with transpose=True")
         if tuple(bias.shape) != (n_out,) or bias.dtype != torch.bfloat16:
             raise ValueError(f"[{op}] bias must be bfloat16 of shape ({n_out},)")
-    y = torch.empty(tuple(x.shape[:-1]) + (n_out,), dtype=torch.bfloat16, device=x.device)
+    shape = tuple(x.shape[:-1]) + (n_out,)
+    if accumulate is not None:
+        _need_cuda(op, accumulate=accumulate)
+        if (tuple(accumulate.shape) != shape or accumulate.dtype != torch.bfloat16
+                or not accumulate.is_contiguous() or accumulate.device != x.device):
+            raise ValueError(f"[{op}] accumulate must be a contiguous bfloat16 tensor of shape "
+                             f"{shape} on {x.device}")
+        y = accumulate
+        entry = lib().tq_qlora_matmul_accumulate
+    else:
+        y = torch.empty(shape, dtype=torch.bfloat16, device=x.device)
+        entry = lib().tq_qlora_matmul_ws
     up = lora_up.contiguous() if lora_up is not None else None
     if lora_down is None:
         down = None
@@ -382,7 +397,7 @@ def qlora_matmul(x: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, biase
     with torch.cuda.device(x.device):
         ws, ws_bytes = _workspace(x2.shape[0], w_rows, w_cols, transpose, group_size, bits,
                                   x.device)
-        _launch("qmm", lambda: lib().tq_qlora_matmul_ws(
+        _launch("qmm", lambda: entry(
             _ptr(x2), _ptr(w_q.contiguous()), _ptr(scales.contiguous()), _ptr(biases.contiguous()),
             x2.shape[0], w_rows, w_cols, 1 if transpose else 0, group_size, bits, _ptr(b), _ptr(up),
             _ptr(down), ld_down, rank, _ptr(y), _ptr(ws), ws_bytes, _stream()),

@@ -295,12 +295,12 @@ class _QLoRAGroup(torch.autograd.Function):
                 up_g, _ = ops.lora_down(dy2, ad.bt16, ad.scale, out_t=u_t[rows])
                 ops.lora_grad(dy2, down_t[rows], 0, out=ad.gb, accumulate=True)
                 if need_dx:
-                    d = ops.qlora_matmul(dy2, w.codes, w.scales, w.biases, False, w.group, w.bits,
-                                         lora_up=ad.a16, lora_down=up_g)
-                    dx = d if dx is None else dx.add_(d)
+                    # Members after the first add their dX in the GEMM's epilogue.
+                    dx = ops.qlora_matmul(dy2, w.codes, w.scales, w.biases, False, w.group,
+                                          w.bits, lora_up=ad.a16, lora_down=up_g, accumulate=dx)
             elif need_dx:
-                d = ops.quantized_matmul(dy2, w.codes, w.scales, w.biases, False, w.group, w.bits)
-                dx = d if dx is None else dx.add_(d)
+                dx = ops.qlora_matmul(dy2, w.codes, w.scales, w.biases, False, w.group, w.bits,
+                                      accumulate=dx)
         ops.lora_grad(x2, u_t, 1, out=group.ga, accumulate=True)
         if dx is not None:
             dx = dx.view(ctx.in_shape)
