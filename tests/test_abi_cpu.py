@@ -135,3 +135,24 @@ def test_attention_argument_errors_need_no_gpu():
     assert bwd(need.value - 4) == TQ_ERR_INVALID and b"workspace" in L.tq_last_error()
     assert bwd(need.value, ws=p + 16) == TQ_ERR_MISALIGNED and b"256" in L.tq_last_error()
     assert bwd(need.value, ws=0) == TQ_ERR_INVALID and b"null" in L.tq_last_error()
+
+
+def test_integration_bindings_match_the_header():
+    """The Rust extern block a maintainer would paste binds
+    every function of include/torobi_b200.h with the same parameters."""
+    import re
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    header = (root / "include" / "torobi_b200.h").read_text()
+    decl = {}
+    for m in re.finditer(r"^(?:int|const char\*)\s+(tq_\w+)\((.*?)\);", header, flags=re.M | re.S):
+        args = [a.strip() for a in m.group(2).split(",") if a.strip() not in ("", "void")]
+        decl[m.group(1)] = [a.split()[-1].lstrip("*") for a in args]
+    text = (root / "INTEGRATION.md").read_text()
+    rust = {}
+    for m in re.finditer(r"pub fn (tq_\w+)\((.*?)\)\s*->", text, flags=re.S):
+        rust[m.group(1)] = [a.split(":")[0].strip() for a in m.group(2).split(",") if a.strip()]
+    assert set(rust) == set(decl), (set(decl) ^ set(rust))
+    for name, params in decl.items():
+        assert rust[name] == params, name
