@@ -199,6 +199,33 @@ def test_small_token_forward(cuda, oracle, case):
     assert oracle.rel_err(got, want) <= TOL
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape", [(28672, 8192), (65536, 4096)], ids=lambda s: "n{}_k{}".format(*s))
+def test_small_token_forward_repeated(cuda, shape):
+    """Shapes whose small-token launch wraps its six-stage ring and puts two
+    CTAs on an SM, over more than one wave: launched again and again, every
+    result must hold (a stage refilled under pending reads once corrupted
+    one 16-row slab in most such launches).  Reference: the exactly
+    dequantized weight in f32."""
+    import torch
+    import torobi_b200 as tq
+
+    n, k = shape
+    g = torch.Generator(device=cuda)
+    g.manual_seed(n + k)
+    w = (torch.randn(n, k, device=cuda, generator=g) * 0.02).bfloat16()
+    c, s, b = tq.quantize(w, 64, 4)
+    wd = tq.dequantize(c, s, b, 64, 4).float()
+    del w
+    for m in (1, 8):
+        for _ in range(8):
+            x = torch.randn(m, k, device=cuda, generator=g).bfloat16()
+            y = tq.quantized_matmul(x, c, s, b, True, 64, 4).float()
+            ref = x.float() @ wd.t()
+            err = ((y - ref).abs().max() / ref.abs().max()).item()
+            assert err <= TOL, (m, err)
+
+
 # The quantized_matmul shape sweep: Llama-3-8B projections (4096x4096,
 # 1024x4096, 14336x4096, 4096x14336) and Llama-3-70B ones (8192x8192,
 # 28672x8192, 8192x28672) as (w_rows, w_cols), 4-bit group 64, weights

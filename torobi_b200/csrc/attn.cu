@@ -177,6 +177,10 @@ __global__ void __launch_bounds__(384, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot_ptr;
+  // Signalled only once this CTA holds its tensor memory: a dependent
+  // kernel's CTA placed on this SM may then wait for it, never hold it.
+  griddep_launch_dependents();
+  griddep_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------- TMA
@@ -473,6 +477,8 @@ struct PrepParams {
 
 // Eight lanes per row, dim / 8 elements each.
 __global__ void __launch_bounds__(256) attn_bwd_prep_kernel(const PrepParams p) {
+  griddep_wait();
+  griddep_launch_dependents();
   const long long gid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long row = gid >> 3;
   const int sub = threadIdx.x & 7;
@@ -626,6 +632,10 @@ __global__ void __launch_bounds__(384, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot_ptr;
+  // Signalled only once this CTA holds its tensor memory: a dependent
+  // kernel's CTA placed on this SM may then wait for it, never hold it.
+  griddep_launch_dependents();
+  griddep_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------- TMA
@@ -898,6 +908,10 @@ __global__ void __launch_bounds__(384, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot_ptr;
+  // Signalled only once this CTA holds its tensor memory: a dependent
+  // kernel's CTA placed on this SM may then wait for it, never hold it.
+  griddep_launch_dependents();
+  griddep_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------- TMA
@@ -1039,6 +1053,9 @@ __global__ void __launch_bounds__(384, 1)
         dk[i / 2] = pack_bf16x2_f32(dsv[0], dsv[1]);
         dk[i / 2 + 1] = pack_bf16x2_f32(dsv[2], dsv[3]);
       }
+      // The stat reads above are ordered before the copies that refill the
+      // stage (generic-proxy reads, async-proxy writes).
+      fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(q_empty(s));
       // Row `row` of the K-major operand: 64 bf16 = eight 16-byte chunks,
@@ -1158,8 +1175,8 @@ int launch_fwd(const void* q, const void* k, const void* v, const AttnShape& sh,
   p.lse = lse;
   p.status = status;
   const unsigned grid = static_cast<unsigned>(sh.batch) * sh.heads * p.n_pairs;
-  attn_fwd_kernel<D><<<grid, 384, C::SMEM, stream>>>(tq_, tk, tv, p);
-  return check_cuda(cudaGetLastError(), "attention forward launch");
+  return launch_kernel(attn_fwd_kernel<D>, dim3(grid), dim3(384), C::SMEM, stream, 1,
+                       "attention forward launch", tq_, tk, tv, p);
 }
 
 template <int D>
@@ -1186,8 +1203,8 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* out, con
   pp.seq_pad = seq_pad;
   pp.dim = D;
   const long long rows = static_cast<long long>(sh.batch) * sh.heads * seq_pad;
-  attn_bwd_prep_kernel<<<static_cast<unsigned>((rows * 8 + 255) / 256), 256, 0, stream>>>(pp);
-  rc = check_cuda(cudaGetLastError(), "attention backward prep launch");
+  rc = launch_kernel(attn_bwd_prep_kernel, dim3(static_cast<unsigned>((rows * 8 + 255) / 256)),
+                     dim3(256), 0, stream, 1, "attention backward prep launch", pp);
   if (rc) return rc;
   // Query-side maps (128-row boxes for dq, 64-row boxes for dkv) and the
   // key/value maps the other way round.
@@ -1211,12 +1228,12 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* out, con
   p.dv = static_cast<uint16_t*>(dv);
   p.status = status;
   const unsigned grid_q = static_cast<unsigned>(sh.batch) * sh.heads * sh.n_tiles;
-  attn_bwd_dq_kernel<D><<<grid_q, 384, Q::SMEM, stream>>>(q128, do128, k64, v64, p);
-  rc = check_cuda(cudaGetLastError(), "attention backward dq launch");
+  rc = launch_kernel(attn_bwd_dq_kernel<D>, dim3(grid_q), dim3(384), Q::SMEM, stream, 1,
+                     "attention backward dq launch", q128, do128, k64, v64, p);
   if (rc) return rc;
   const unsigned grid_kv = static_cast<unsigned>(sh.batch) * sh.kv_heads * sh.n_tiles;
-  attn_bwd_dkv_kernel<D><<<grid_kv, 384, KV::SMEM, stream>>>(q64, do64, k128, v128, p);
-  return check_cuda(cudaGetLastError(), "attention backward dkv launch");
+  return launch_kernel(attn_bwd_dkv_kernel<D>, dim3(grid_kv), dim3(384), KV::SMEM, stream, 1,
+                       "attention backward dkv launch", q64, do64, k128, v128, p);
 }
 
 }  // namespace

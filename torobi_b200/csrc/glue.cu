@@ -52,6 +52,8 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const uint4* __restric
                                                           uint4* __restrict__ s_out,
                                                           uint4* __restrict__ y,
                                                           float* __restrict__ rstd) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -103,6 +105,8 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const uint4* __restric
                                                           const uint4* __restrict__ dres,
                                                           int64_t rows, int hv,
                                                           uint4* __restrict__ dx) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -152,6 +156,8 @@ __global__ void __launch_bounds__(256) rope_kernel(const uint4* __restrict__ x, 
                                                    const float* __restrict__ cosv,
                                                    const float* __restrict__ sinv, float sign,
                                                    uint4* __restrict__ y) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int half = dim / 2;
   const I per_head = static_cast<I>(half / 8);  // threads per head
   const I n = static_cast<I>(tokens) * static_cast<I>(heads) * per_head;
@@ -187,6 +193,8 @@ __device__ __forceinline__ float sigmoidf_(float v) { return 1.0f / (1.0f + __ex
 __global__ void __launch_bounds__(256) swiglu_fwd_kernel(const uint4* __restrict__ g,
                                                          const uint4* __restrict__ u, int64_t nv,
                                                          uint4* __restrict__ a) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nv; i += stride) {
     float fg[8], fu[8], o[8];
@@ -203,6 +211,8 @@ __global__ void __launch_bounds__(256) swiglu_bwd_kernel(const uint4* __restrict
                                                          const uint4* __restrict__ da, int64_t nv,
                                                          uint4* __restrict__ dg,
                                                          uint4* __restrict__ du) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nv; i += stride) {
     float fg[8], fu[8], fd[8], og[8], ou[8];
@@ -250,10 +260,10 @@ extern "C" int tq_rmsnorm_fwd(const void* x, const void* w, int64_t rows, int64_
     return fail(TQ_ERR_MISALIGNED, "rmsnorm: x, w and y must be 16-byte aligned");
   const int warps = 8;
   const unsigned grid = static_cast<unsigned>((rows + warps - 1) / warps);
-  rmsnorm_fwd_kernel<false><<<grid, warps * 32, 0, as_stream(stream)>>>(
-      static_cast<const uint4*>(x), nullptr, static_cast<const uint4*>(w), rows,
-      static_cast<int>(hidden / 8), eps, nullptr, static_cast<uint4*>(y), rstd);
-  return check_cuda(cudaGetLastError(), "rmsnorm_fwd launch");
+  return launch_kernel(rmsnorm_fwd_kernel<false>, dim3(grid), dim3(warps * 32), 0,
+                       as_stream(stream), 1, "rmsnorm_fwd launch", static_cast<const uint4*>(x),
+                       nullptr, static_cast<const uint4*>(w), rows, static_cast<int>(hidden / 8),
+                       eps, nullptr, static_cast<uint4*>(y), rstd);
 }
 
 extern "C" int tq_add_rmsnorm_fwd(const void* x, const void* res, const void* w, int64_t rows,
@@ -276,11 +286,11 @@ extern "C" int tq_add_rmsnorm_fwd(const void* x, const void* res, const void* w,
                 "add_rmsnorm: s and y must not overlap x, res or each other (no in-place form)");
   const int warps = 8;
   const unsigned grid = static_cast<unsigned>((rows + warps - 1) / warps);
-  rmsnorm_fwd_kernel<true><<<grid, warps * 32, 0, as_stream(stream)>>>(
-      static_cast<const uint4*>(x), static_cast<const uint4*>(res), static_cast<const uint4*>(w),
-      rows, static_cast<int>(hidden / 8), eps, static_cast<uint4*>(s), static_cast<uint4*>(y),
-      rstd);
-  return check_cuda(cudaGetLastError(), "add_rmsnorm_fwd launch");
+  return launch_kernel(rmsnorm_fwd_kernel<true>, dim3(grid), dim3(warps * 32), 0,
+                       as_stream(stream), 1, "add_rmsnorm_fwd launch",
+                       static_cast<const uint4*>(x), static_cast<const uint4*>(res),
+                       static_cast<const uint4*>(w), rows, static_cast<int>(hidden / 8), eps,
+                       static_cast<uint4*>(s), static_cast<uint4*>(y), rstd);
 }
 
 extern "C" int tq_rmsnorm_bwd(const void* x, const void* w, const float* rstd, const void* dy,
@@ -296,11 +306,11 @@ extern "C" int tq_rmsnorm_bwd(const void* x, const void* w, const float* rstd, c
     return fail(TQ_ERR_MISALIGNED, "rmsnorm: tensors must be 16-byte aligned");
   const int warps = 8;
   const unsigned grid = static_cast<unsigned>((rows + warps - 1) / warps);
-  rmsnorm_bwd_kernel<<<grid, warps * 32, 0, as_stream(stream)>>>(
-      static_cast<const uint4*>(x), static_cast<const uint4*>(w), rstd,
-      static_cast<const uint4*>(dy), static_cast<const uint4*>(dres), rows,
-      static_cast<int>(hidden / 8), static_cast<uint4*>(dx));
-  return check_cuda(cudaGetLastError(), "rmsnorm_bwd launch");
+  return launch_kernel(rmsnorm_bwd_kernel, dim3(grid), dim3(warps * 32), 0, as_stream(stream), 1,
+                       "rmsnorm_bwd launch", static_cast<const uint4*>(x),
+                       static_cast<const uint4*>(w), rstd, static_cast<const uint4*>(dy),
+                       static_cast<const uint4*>(dres), rows, static_cast<int>(hidden / 8),
+                       static_cast<uint4*>(dx));
 }
 
 extern "C" int tq_rope(const void* x, int64_t tokens, int64_t heads, int64_t dim, int64_t seq,
@@ -319,15 +329,12 @@ extern "C" int tq_rope(const void* x, int64_t tokens, int64_t heads, int64_t dim
   const int64_t n = tokens * heads * (dim / 16);
   const int grid = grid_for(n, 256);
   // 32-bit indices while every index the grid-stride loop forms fits.
-  if (n + static_cast<int64_t>(grid) * 256 < (1ll << 32))
-    rope_kernel<uint32_t><<<grid, 256, 0, as_stream(stream)>>>(
-        static_cast<const uint4*>(x), tokens, static_cast<int>(heads), static_cast<int>(dim),
-        static_cast<int>(seq), cosv, sinv, inverse ? -1.0f : 1.0f, static_cast<uint4*>(y));
-  else
-    rope_kernel<int64_t><<<grid, 256, 0, as_stream(stream)>>>(
-        static_cast<const uint4*>(x), tokens, static_cast<int>(heads), static_cast<int>(dim),
-        static_cast<int>(seq), cosv, sinv, inverse ? -1.0f : 1.0f, static_cast<uint4*>(y));
-  return check_cuda(cudaGetLastError(), "rope launch");
+  auto kernel = n + static_cast<int64_t>(grid) * 256 < (1ll << 32) ? rope_kernel<uint32_t>
+                                                                    : rope_kernel<int64_t>;
+  return launch_kernel(kernel, dim3(grid), dim3(256), 0, as_stream(stream), 1, "rope launch",
+                       static_cast<const uint4*>(x), tokens, static_cast<int>(heads),
+                       static_cast<int>(dim), static_cast<int>(seq), cosv, sinv,
+                       inverse ? -1.0f : 1.0f, static_cast<uint4*>(y));
 }
 
 extern "C" int tq_swiglu_fwd(const void* g, const void* u, int64_t n, void* a, void* stream) {
@@ -337,9 +344,9 @@ extern "C" int tq_swiglu_fwd(const void* g, const void* u, int64_t n, void* a, v
   if (n == 0) return TQ_OK;
   if (!g || !u || !a) return fail(TQ_ERR_INVALID, "swiglu: null pointer");
   if (!a16(g) || !a16(u) || !a16(a)) return fail(TQ_ERR_MISALIGNED, "swiglu: 16-byte alignment");
-  swiglu_fwd_kernel<<<grid_for(n / 8, 256), 256, 0, as_stream(stream)>>>(
-      static_cast<const uint4*>(g), static_cast<const uint4*>(u), n / 8, static_cast<uint4*>(a));
-  return check_cuda(cudaGetLastError(), "swiglu_fwd launch");
+  return launch_kernel(swiglu_fwd_kernel, dim3(grid_for(n / 8, 256)), dim3(256), 0,
+                       as_stream(stream), 1, "swiglu_fwd launch", static_cast<const uint4*>(g),
+                       static_cast<const uint4*>(u), n / 8, static_cast<uint4*>(a));
 }
 
 extern "C" int tq_swiglu_bwd(const void* g, const void* u, const void* da, int64_t n, void* dg,
@@ -351,8 +358,8 @@ extern "C" int tq_swiglu_bwd(const void* g, const void* u, const void* da, int64
   if (!g || !u || !da || !dg || !du) return fail(TQ_ERR_INVALID, "swiglu: null pointer");
   if (!a16(g) || !a16(u) || !a16(da) || !a16(dg) || !a16(du))
     return fail(TQ_ERR_MISALIGNED, "swiglu: 16-byte alignment");
-  swiglu_bwd_kernel<<<grid_for(n / 8, 256), 256, 0, as_stream(stream)>>>(
-      static_cast<const uint4*>(g), static_cast<const uint4*>(u), static_cast<const uint4*>(da),
-      n / 8, static_cast<uint4*>(dg), static_cast<uint4*>(du));
-  return check_cuda(cudaGetLastError(), "swiglu_bwd launch");
+  return launch_kernel(swiglu_bwd_kernel, dim3(grid_for(n / 8, 256)), dim3(256), 0,
+                       as_stream(stream), 1, "swiglu_bwd launch", static_cast<const uint4*>(g),
+                       static_cast<const uint4*>(u), static_cast<const uint4*>(da), n / 8,
+                       static_cast<uint4*>(dg), static_cast<uint4*>(du));
 }

@@ -122,6 +122,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot_ptr;
+  // Signalled only once this CTA holds its tensor memory: a dependent
+  // kernel's CTA placed on this SM may then wait for it, never hold it.
+  griddep_launch_dependents();
+  griddep_wait();
 
   if (warp == 0) {
     if (elect_one_sync()) {
@@ -292,24 +296,13 @@ int launch_skinny_nb(const CUtensorMap& tm_a, const CUtensorMap& tm_b, const Ski
                      int64_t tiles, int64_t split, cudaStream_t stream) {
   using C = SkinnyCfg<NB>;
   const dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>(split), 1);
-  if (GRAD || split == 1) {
-    skinny_kernel<GRAD, NB><<<grid, kThreads, C::SMEM, stream>>>(tm_a, tm_b, p);
-    return check_cuda(cudaGetLastError(), GRAD ? "lora_grad launch" : "lora_down launch");
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = static_cast<size_t>(C::SMEM + (split - 1) * C::PART_BYTES);
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = static_cast<unsigned>(split);
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return check_cuda(cudaLaunchKernelEx(&cfg, skinny_kernel<GRAD, NB>, tm_a, tm_b, p),
-                    "lora_down launch");
+  if (GRAD || split == 1)
+    return launch_kernel(skinny_kernel<GRAD, NB>, grid, dim3(kThreads), C::SMEM, stream, 1,
+                         GRAD ? "lora_grad launch" : "lora_down launch", tm_a, tm_b, p);
+  return launch_kernel(skinny_kernel<GRAD, NB>, grid, dim3(kThreads),
+                       static_cast<size_t>(C::SMEM + (split - 1) * C::PART_BYTES), stream,
+                       dim3(1, static_cast<unsigned>(split), 1), "lora_down launch", tm_a, tm_b,
+                       p);
 }
 
 template <bool GRAD>

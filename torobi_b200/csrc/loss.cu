@@ -90,6 +90,8 @@ __global__ void __launch_bounds__(kCeThreads) ce_fwd_kernel(const uint16_t* __re
                                                             int vocab, int64_t ld,
                                                             float* __restrict__ lse,
                                                             float* __restrict__ loss) {
+  griddep_wait();
+  griddep_launch_dependents();
   __shared__ MaxSum sh[kCeThreads / 32];
   const int64_t r = blockIdx.x;
   const uint16_t* row = z + r * ld;
@@ -123,6 +125,8 @@ __global__ void __launch_bounds__(kCeThreads) ce_bwd_kernel(const uint16_t* z,
                                                             int vocab, int64_t ld,
                                                             const float* __restrict__ dloss,
                                                             float scale, uint16_t* dz) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int64_t r = blockIdx.x;
   const uint16_t* row = z + r * ld;
   uint16_t* out = dz + r * ld;
@@ -190,11 +194,9 @@ extern "C" int tq_cross_entropy_fwd(const void* logits, const int64_t* targets, 
   const uint16_t* z = static_cast<const uint16_t*>(logits);
   const int v = static_cast<int>(vocab);
   const unsigned grid = static_cast<unsigned>(rows);
-  if (ce_vec(logits, logits, vocab, ld))
-    ce_fwd_kernel<true><<<grid, kCeThreads, 0, as_stream(stream)>>>(z, targets, v, ld, lse, loss);
-  else
-    ce_fwd_kernel<false><<<grid, kCeThreads, 0, as_stream(stream)>>>(z, targets, v, ld, lse, loss);
-  return check_cuda(cudaGetLastError(), "cross_entropy_fwd launch");
+  auto kernel = ce_vec(logits, logits, vocab, ld) ? ce_fwd_kernel<true> : ce_fwd_kernel<false>;
+  return launch_kernel(kernel, dim3(grid), dim3(kCeThreads), 0, as_stream(stream), 1,
+                       "cross_entropy_fwd launch", z, targets, v, ld, lse, loss);
 }
 
 extern "C" int tq_cross_entropy_bwd(const void* logits, const int64_t* targets, const float* lse,
@@ -211,11 +213,7 @@ extern "C" int tq_cross_entropy_bwd(const void* logits, const int64_t* targets, 
   uint16_t* dz = static_cast<uint16_t*>(dlogits);
   const int v = static_cast<int>(vocab);
   const unsigned grid = static_cast<unsigned>(rows);
-  if (ce_vec(logits, dlogits, vocab, ld))
-    ce_bwd_kernel<true><<<grid, kCeThreads, 0, as_stream(stream)>>>(z, targets, lse, v, ld, dloss,
-                                                                    scale, dz);
-  else
-    ce_bwd_kernel<false><<<grid, kCeThreads, 0, as_stream(stream)>>>(z, targets, lse, v, ld, dloss,
-                                                                     scale, dz);
-  return check_cuda(cudaGetLastError(), "cross_entropy_bwd launch");
+  auto kernel = ce_vec(logits, dlogits, vocab, ld) ? ce_bwd_kernel<true> : ce_bwd_kernel<false>;
+  return launch_kernel(kernel, dim3(grid), dim3(kCeThreads), 0, as_stream(stream), 1,
+                       "cross_entropy_bwd launch", z, targets, lse, v, ld, dloss, scale, dz);
 }

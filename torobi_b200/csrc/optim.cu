@@ -12,6 +12,8 @@ namespace {
 
 __global__ void __launch_bounds__(256) sumsq_kernel(const float* __restrict__ x, int64_t n,
                                                     float* __restrict__ out) {
+  griddep_wait();
+  griddep_launch_dependents();
   float acc = 0.0f;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const int64_t n4 = n / 4;
@@ -57,6 +59,8 @@ __global__ void __launch_bounds__(256) adamw_kernel(float* __restrict__ params,
                                                     int64_t n, AdamArgs a,
                                                     const float* __restrict__ norm_sq,
                                                     uint16_t* __restrict__ params_bf16) {
+  griddep_wait();
+  griddep_launch_dependents();
   float gscale = a.grad_scale;
   if (norm_sq) {
     const float ns = *norm_sq;
@@ -102,6 +106,8 @@ __global__ void __launch_bounds__(256) adamw_kernel(float* __restrict__ params,
 // dst[c, r] = bf16(src[r, c]) through a 32x33 shared tile.
 __global__ void transpose_bf16_kernel(const float* __restrict__ src, int64_t rows, int64_t cols,
                                       uint16_t* __restrict__ dst) {
+  griddep_wait();
+  griddep_launch_dependents();
   __shared__ float tile[32][33];
   const int64_t r0 = static_cast<int64_t>(blockIdx.y) * 32;
   const int64_t c0 = static_cast<int64_t>(blockIdx.x) * 32;
@@ -138,8 +144,8 @@ extern "C" int tq_sumsq(const float* x, int64_t n, float* out, int accumulate, v
   }
   if (n == 0) return TQ_OK;
   if (!x || !aligned(x, 16)) return fail(TQ_ERR_MISALIGNED, "x must be non-null and 16-byte aligned");
-  sumsq_kernel<<<grid_for(n / 4 + 1, 256), 256, 0, s>>>(x, n, out);
-  return check_cuda(cudaGetLastError(), "sumsq launch");
+  return launch_kernel(sumsq_kernel, dim3(grid_for(n / 4 + 1, 256)), dim3(256), 0, s, 1,
+                       "sumsq launch", x, n, out);
 }
 
 extern "C" int tq_adamw(float* params, const float* grads, float* m, float* v, int64_t n, int64_t t,
@@ -165,9 +171,9 @@ extern "C" int tq_adamw(float* params, const float* grads, float* m, float* v, i
   a.bias1 = 1.0f - powf(beta1, static_cast<float>(t));
   a.bias2 = 1.0f - powf(beta2, static_cast<float>(t));
   a.clip = clip;
-  adamw_kernel<<<grid_for(n / 4 + 1, 256), 256, 0, as_stream(stream)>>>(
-      params, grads, m, v, n, a, norm_sq, static_cast<uint16_t*>(params_bf16));
-  return check_cuda(cudaGetLastError(), "adamw launch");
+  return launch_kernel(adamw_kernel, dim3(grid_for(n / 4 + 1, 256)), dim3(256), 0,
+                       as_stream(stream), 1, "adamw launch", params, grads, m, v, n, a, norm_sq,
+                       static_cast<uint16_t*>(params_bf16));
 }
 
 extern "C" int tq_transpose_to_bf16(const float* src, int64_t rows, int64_t cols, void* dst,
@@ -178,7 +184,6 @@ extern "C" int tq_transpose_to_bf16(const float* src, int64_t rows, int64_t cols
   if (!src || !dst) return fail(TQ_ERR_INVALID, "null pointer");
   const dim3 block(32, 8);
   const dim3 grid(static_cast<unsigned>((cols + 31) / 32), static_cast<unsigned>((rows + 31) / 32));
-  transpose_bf16_kernel<<<grid, block, 0, as_stream(stream)>>>(src, rows, cols,
-                                                               static_cast<uint16_t*>(dst));
-  return check_cuda(cudaGetLastError(), "transpose launch");
+  return launch_kernel(transpose_bf16_kernel, grid, block, 0, as_stream(stream), 1,
+                       "transpose launch", src, rows, cols, static_cast<uint16_t*>(dst));
 }

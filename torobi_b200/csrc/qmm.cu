@@ -391,6 +391,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot_ptr;
+  // Signalled only once this CTA holds its tensor memory: a dependent
+  // kernel's CTA placed on this SM may then wait for it, never hold it.
+  griddep_launch_dependents();
+  griddep_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -850,6 +854,8 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
                                                             int splits, int64_t m, int n,
                                                             const uint16_t* __restrict__ bias,
                                                             int acc_y, uint16_t* __restrict__ y) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int64_t nv = m * n / 8;
   const int64_t plane = m * n;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -1028,16 +1034,16 @@ int launch(const Args& a, const Plan& pl, cudaStream_t stream, int* status) {
   if (rc) return rc;
   const int units = p.tiles_total * p.splits;
   const int grid = units < sm_count() ? units : sm_count();
-  kernel<<<grid, kThreads, C::SMEM, stream>>>(mp.x, mp.c, mp.lup, mp.ldn, mp.sc, mp.bi, tm_y, p);
-  rc = check_cuda(cudaGetLastError(), "qmm launch");
+  rc = launch_kernel(kernel, dim3(grid), dim3(kThreads), C::SMEM, stream, 1, "qmm launch", mp.x,
+                     mp.c, mp.lup, mp.ldn, mp.sc, mp.bi, tm_y, p);
   if (rc || pl.splits == 1) return rc;
   const int64_t nv = a.m * n_out / 8;
   int rgrid = static_cast<int>((nv + 255) / 256);
   if (rgrid > sm_count() * 8) rgrid = sm_count() * 8;
-  splitk_reduce_kernel<<<rgrid, 256, 0, stream>>>(
-      static_cast<const float*>(a.ws), pl.splits, a.m, static_cast<int>(n_out),
-      static_cast<const uint16_t*>(a.bias), a.acc, static_cast<uint16_t*>(a.y));
-  return check_cuda(cudaGetLastError(), "split-K reduce launch");
+  return launch_kernel(splitk_reduce_kernel, dim3(rgrid), dim3(256), 0, stream, 1,
+                       "split-K reduce launch", static_cast<const float*>(a.ws), pl.splits, a.m,
+                       static_cast<int>(n_out), static_cast<const uint16_t*>(a.bias), a.acc,
+                       static_cast<uint16_t*>(a.y));
 }
 
 template <int BITS, bool TRANS, int BN>
@@ -1104,21 +1110,8 @@ int launch_pair(const Args& a, const Plan& pl, cudaStream_t stream, int* status)
   if (rc) return rc;
   const int pairs = resident_pairs(kernel, C::SMEM);
   const int grid_pairs = p.tiles_total < pairs ? p.tiles_total : pairs;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * grid_pairs, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = static_cast<size_t>(C::SMEM);
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return check_cuda(
-      cudaLaunchKernelEx(&cfg, kernel, mp.x, mp.c, mp.lup, mp.ldn, mp.sc, mp.bi, tm_y, p),
-      "qmm pair launch");
+  return launch_kernel(kernel, dim3(2 * grid_pairs), dim3(kThreads), C::SMEM, stream, dim3(2),
+                       "qmm pair launch", mp.x, mp.c, mp.lup, mp.ldn, mp.sc, mp.bi, tm_y, p);
 }
 
 template <int BITS, int BN>
@@ -1143,21 +1136,8 @@ int launch_pair_ts(const Args& a, const Plan& pl, cudaStream_t stream, int* stat
   if (rc) return rc;
   const int pairs = resident_pairs(kernel, C::SMEM);
   const int grid_pairs = p.tiles_total < pairs ? p.tiles_total : pairs;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * grid_pairs, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = static_cast<size_t>(C::SMEM);
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return check_cuda(
-      cudaLaunchKernelEx(&cfg, kernel, mp.x, mp.c, mp.lup, mp.ldn, mp.sc, mp.bi, tm_y, p),
-      "qmm pair ts launch");
+  return launch_kernel(kernel, dim3(2 * grid_pairs), dim3(kThreads), C::SMEM, stream, dim3(2),
+                       "qmm pair ts launch", mp.x, mp.c, mp.lup, mp.ldn, mp.sc, mp.bi, tm_y, p);
 }
 
 template <int BITS, bool TRANS>
@@ -1227,20 +1207,10 @@ int launch_small_mt(const Args& a, const Plan& pl, cudaStream_t stream, int* sta
   p.cs = pl.small_cs;
   p.status = status;
   const int64_t blocks = (a.w_rows + kSmallRows - 1) / kSmallRows;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(blocks * pl.small_cs), 1, 1);
-  cfg.blockDim = dim3(kSmallThreads, 1, 1);
-  cfg.dynamicSmemBytes = static_cast<size_t>(C::smem(pl.small_cs));
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(pl.small_cs);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pl.small_cs > 1 ? 1 : 0;
-  return check_cuda(cudaLaunchKernelEx(&cfg, qmm_small_kernel<MT>, tm_x, tm_c, p),
-                    "quantized_matmul (small) launch");
+  return launch_kernel(qmm_small_kernel<MT>, dim3(static_cast<unsigned>(blocks * pl.small_cs)),
+                       dim3(kSmallThreads), static_cast<size_t>(C::smem(pl.small_cs)), stream,
+                       dim3(static_cast<unsigned>(pl.small_cs)), "quantized_matmul (small) launch",
+                       tm_x, tm_c, p);
 }
 
 int launch_small(const Args& a, const Plan& pl, cudaStream_t stream, int* status) {

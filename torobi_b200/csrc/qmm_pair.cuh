@@ -174,6 +174,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot_ptr;
+  // Signalled only once this CTA holds its tensor memory: a dependent
+  // kernel's CTA placed on this SM may then wait for it, never hold it.
+  griddep_launch_dependents();
+  griddep_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -330,7 +334,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     // two staging buffers ([token][feature] bf16) and out by a TMA store,
     // which clips tokens past m and features past n_out.
     const int q = warp & 3;
-    const int r = q * 32 + lane;
     const uint32_t stage_w = epi + static_cast<uint32_t>(q) * 2 * C::EPI_CHUNK;
     if (lane == 0) tma_prefetch_desc(&tm_y);
     bool ok = true;

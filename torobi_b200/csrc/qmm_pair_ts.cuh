@@ -176,6 +176,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot_ptr;
+  // Signalled only once this CTA holds its tensor memory: a dependent
+  // kernel's CTA placed on this SM may then wait for it, never hold it.
+  griddep_launch_dependents();
+  griddep_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -315,6 +319,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_st_32x32b_x32(tmem + lane_base + C::A_COL0 + a * C::A_COLS, v);
         tmem_st_wait();
         tc_fence_before();
+        // The code and scale reads of the stage are ordered before the TMA
+        // that refills it once the MMA has committed.
+        fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(lead(aready_b(a)));
       }

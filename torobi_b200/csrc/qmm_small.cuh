@@ -76,6 +76,8 @@ template <int MT>
 __global__ void __launch_bounds__(kSmallThreads, 1)
     qmm_small_kernel(const __grid_constant__ CUtensorMap tm_x,
                      const __grid_constant__ CUtensorMap tm_c, const SmallParams p) {
+  griddep_wait();
+  griddep_launch_dependents();
   using C = SmallCfg<MT>;
   constexpr int XS = kSmallXStages;
   constexpr int D = kSmallDepth;
@@ -198,6 +200,11 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
                 mma_16816_bf16(acc[nt], oa[2], ob[2], oa[3], ob[3], x2, x3);
               }
             }
+            // This warp's reads of the stage are ordered before the TMA
+            // that refills it (generic-proxy reads, async-proxy writes):
+            // without the fence a refill was seen to land under reads still
+            // pending when two CTAs shared an SM.
+            fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(x_empty(s));
             if (c + D < nc) load(d, c + D);

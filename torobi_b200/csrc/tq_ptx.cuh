@@ -209,6 +209,23 @@ __device__ __forceinline__ void tma_store_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
+// ------------------------------------------- programmatic dependent launch --
+// A kernel launched with programmatic stream serialization may start while
+// the previous kernel on its stream is still running: griddep_wait blocks
+// until that kernel has completed and its writes are visible (at once when
+// the launch did not allow overlap).  Every kernel calls it, unconditionally,
+// before its first global-memory access, so a grid that completes implies
+// that the grids before it have too.  griddep_launch_dependents lets the
+// next such kernel be scheduled once every CTA of this one has called it or
+// exited.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // --------------------------------------------------------------- tcgen05 ----
 
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {

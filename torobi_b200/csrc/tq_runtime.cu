@@ -3,6 +3,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -77,6 +78,14 @@ int set_max_smem_once(const void* func, int bytes, const char* what) {
   if (rc) return rc;
   if (n_done < 512) done[n_done++] = Entry{func, dev};
   return TQ_OK;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("TQ_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 int sm_count() {

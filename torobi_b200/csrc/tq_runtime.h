@@ -5,6 +5,7 @@
 
 #include <cstdarg>
 #include <cstdint>
+#include <utility>
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -41,5 +42,41 @@ int sm_count();
 // per (kernel, device): later calls return at once, so a launch inside a
 // stream capture makes no attribute call.
 int set_max_smem_once(const void* func, int bytes, const char* what);
+
+// Whether kernels of the training step are launched with programmatic
+// stream serialization (read once per process; TQ_PDL=0 turns it off).
+bool pdl_enabled();
+
+// Launches `kernel` on `stream`, in clusters of shape `cluster` when that
+// holds more than one CTA, and -- when pdl_enabled() -- allowed to start before the
+// previous kernel on the stream has finished: its CTAs may be scheduled once
+// every CTA of that kernel has signalled (griddep_launch_dependents) or
+// exited, and must call griddep_wait before touching global memory.
+template <typename... KArgs, typename... Args>
+int launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                  cudaStream_t stream, dim3 cluster, const char* what, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (cluster.x * cluster.y * cluster.z > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster.x;
+    attr[n].val.clusterDim.y = cluster.y;
+    attr[n].val.clusterDim.z = cluster.z;
+    ++n;
+  }
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...), what);
+}
 
 }  // namespace tq
