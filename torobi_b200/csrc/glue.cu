@@ -42,9 +42,14 @@ __device__ __forceinline__ float warp_sum(float v) {
 // One warp per row; H % 8 == 0.
 // ADD: the row is s = RNE_bf16(x + res), written to s_out, and the norm is
 // taken of that stored s (the residual add and the norm that follows it in
-// the pre-norm block, in one pass; the second pass recomputes s from x and
-// res rather than reading back its own stores).
-template <bool ADD>
+// the pre-norm block, in one pass).
+// VPL > 0: the row fits in VPL 16-byte vectors a lane (H <= 256 VPL), which
+// stay in registers between the sum of squares and the scaling, so the row
+// is read from memory once; all VPL loads of a lane are in flight together.
+// VPL == 0: any H, the second pass reading the row again (recomputing s from
+// x and res rather than reading back its own stores).  Both give the same
+// bits: the same operations in the same order.
+template <bool ADD, int VPL>
 __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const uint4* __restrict__ x,
                                                           const uint4* __restrict__ res,
                                                           const uint4* __restrict__ w, int64_t rows,
@@ -76,24 +81,72 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const uint4* __restric
     }
   };
   float ss = 0.0f;
-  for (int i = lane; i < hv; i += 32) {
-    float f[8];
-    const uint4 sv = load_row(i, f);
-    if constexpr (ADD) s_out[row * hv + i] = sv;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
-  }
-  ss = warp_sum(ss);
-  const float r = rsqrtf(ss / static_cast<float>(hv * 8) + eps);
-  if (rstd && lane == 0) rstd[row] = r;
   uint4* yr = y + row * hv;
-  for (int i = lane; i < hv; i += 32) {
-    float f[8], g[8];
-    load_row(i, f);
-    bf8_to_f32(__ldg(w + i), g);
+  if constexpr (VPL > 0) {
+    uint4 sv[VPL];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) f[j] = f[j] * r * g[j];
-    yr[i] = f32_to_bf8(f);
+    for (int v = 0; v < VPL; ++v) {
+      const int i = lane + 32 * v;
+      if (i < hv) {
+        if constexpr (ADD) {
+          sv[v] = __ldg(xr + i);
+          const uint4 e = __ldg(rr + i);
+          float f[8], g[8];
+          bf8_to_f32(sv[v], f);
+          bf8_to_f32(e, g);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) f[j] += g[j];
+          sv[v] = f32_to_bf8(f);
+        } else {
+          sv[v] = __ldg(xr + i);
+        }
+      }
+    }
+#pragma unroll
+    for (int v = 0; v < VPL; ++v) {
+      const int i = lane + 32 * v;
+      if (i < hv) {
+        if constexpr (ADD) s_out[row * hv + i] = sv[v];
+        float f[8];
+        bf8_to_f32(sv[v], f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+      }
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / static_cast<float>(hv * 8) + eps);
+    if (rstd && lane == 0) rstd[row] = r;
+#pragma unroll
+    for (int v = 0; v < VPL; ++v) {
+      const int i = lane + 32 * v;
+      if (i < hv) {
+        float f[8], g[8];
+        bf8_to_f32(sv[v], f);
+        bf8_to_f32(__ldg(w + i), g);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[j] = f[j] * r * g[j];
+        yr[i] = f32_to_bf8(f);
+      }
+    }
+  } else {
+    for (int i = lane; i < hv; i += 32) {
+      float f[8];
+      const uint4 sv = load_row(i, f);
+      if constexpr (ADD) s_out[row * hv + i] = sv;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / static_cast<float>(hv * 8) + eps);
+    if (rstd && lane == 0) rstd[row] = r;
+    for (int i = lane; i < hv; i += 32) {
+      float f[8], g[8];
+      load_row(i, f);
+      bf8_to_f32(__ldg(w + i), g);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] = f[j] * r * g[j];
+      yr[i] = f32_to_bf8(f);
+    }
   }
 }
 
@@ -239,6 +292,27 @@ int grid_for(int64_t items, int block, int per_sm = 8) {
 
 bool a16(const void* p) { return p == nullptr || aligned(p, 16); }
 
+// Vectors a lane holds when a row of hv 16-byte vectors stays in registers
+// (0: the row is too long; the kernel then reads it twice).  The backward
+// keeps its two reads: holding x and dy of a 4096-wide row (169 registers)
+// left one block per SM and ran 8192 x 4096 in 102 us against 74.
+int row_vpl(int64_t hv) { return hv <= 128 ? 4 : (hv <= 256 ? 8 : (hv <= 512 ? 16 : 0)); }
+
+template <bool ADD>
+using FwdKernel = void (*)(const uint4*, const uint4*, const uint4*, int64_t, int, float, uint4*,
+                           uint4*, float*);
+
+template <bool ADD>
+FwdKernel<ADD> fwd_kernel_for(int64_t hv) {
+  switch (row_vpl(hv)) {
+    case 4: return rmsnorm_fwd_kernel<ADD, 4>;
+    case 8: return rmsnorm_fwd_kernel<ADD, 8>;
+    case 16: return rmsnorm_fwd_kernel<ADD, 16>;
+    default: return rmsnorm_fwd_kernel<ADD, 0>;
+  }
+}
+
+
 // Whether the byte ranges [a, a + n) and [b, b + n) share a byte.
 bool overlap(const void* a, const void* b, size_t n) {
   const uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
@@ -260,7 +334,7 @@ extern "C" int tq_rmsnorm_fwd(const void* x, const void* w, int64_t rows, int64_
     return fail(TQ_ERR_MISALIGNED, "rmsnorm: x, w and y must be 16-byte aligned");
   const int warps = 8;
   const unsigned grid = static_cast<unsigned>((rows + warps - 1) / warps);
-  return launch_kernel(rmsnorm_fwd_kernel<false>, dim3(grid), dim3(warps * 32), 0,
+  return launch_kernel(fwd_kernel_for<false>(hidden / 8), dim3(grid), dim3(warps * 32), 0,
                        as_stream(stream), 1, "rmsnorm_fwd launch", static_cast<const uint4*>(x),
                        nullptr, static_cast<const uint4*>(w), rows, static_cast<int>(hidden / 8),
                        eps, nullptr, static_cast<uint4*>(y), rstd);
@@ -286,7 +360,7 @@ extern "C" int tq_add_rmsnorm_fwd(const void* x, const void* res, const void* w,
                 "add_rmsnorm: s and y must not overlap x, res or each other (no in-place form)");
   const int warps = 8;
   const unsigned grid = static_cast<unsigned>((rows + warps - 1) / warps);
-  return launch_kernel(rmsnorm_fwd_kernel<true>, dim3(grid), dim3(warps * 32), 0,
+  return launch_kernel(fwd_kernel_for<true>(hidden / 8), dim3(grid), dim3(warps * 32), 0,
                        as_stream(stream), 1, "add_rmsnorm_fwd launch",
                        static_cast<const uint4*>(x), static_cast<const uint4*>(res),
                        static_cast<const uint4*>(w), rows, static_cast<int>(hidden / 8), eps,
