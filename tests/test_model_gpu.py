@@ -274,3 +274,54 @@ def test_graph_replayed_steps_match_eager_steps(cuda):
     (l0, p0), (l1, p1) = runs
     assert all(abs(a - b) <= 1e-5 * abs(a) for a, b in zip(l0, l1)), (l0, l1)
     assert torch.allclose(p0, p1, rtol=0, atol=1e-5)
+
+
+_PDL_SCRIPT = r"""
+import sys
+sys.path.insert(0, sys.argv[1])
+import torch
+from torobi_b200.model import QLoRACausalLM, tiny_config
+from torobi_b200.train import AdamWConfig, Trainer
+cuda = torch.device("cuda", 0)
+# Wide enough that the GEMMs run on CTA pairs and the small-token kernel is
+# not used: 2048 tokens, hidden 1024, seven adapted projections.
+cfg = tiny_config(vocab=4096, hidden=1024, intermediate=2816, heads=8, kv_heads=2,
+                  head_dim=128, attention_bias=False, lora_rank=16, lora_alpha=32.0,
+                  lora_targets=("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj",
+                                "up_proj", "down_proj"))
+g = torch.Generator(device=cuda).manual_seed(5)
+batches = [torch.randint(0, cfg.vocab, (4, 512), device=cuda, generator=g) for _ in range(3)]
+model = QLoRACausalLM(cfg, device=cuda, seed=13)
+tr = Trainer(model, AdamWConfig(lr=1e-3), micro_batch=2)
+losses = [float(tr.step(b)) for b in batches]
+torch.save({"losses": losses, "params": model.store.params.cpu()}, sys.argv[2])
+"""
+
+
+@pytest.mark.gpu
+def test_steps_match_without_programmatic_dependent_launch(tmp_path):
+    """Every kernel of the step waits on its predecessor (griddepcontrol)
+    before touching memory, so launching with programmatic dependent launch
+    (the default) or without it (TQ_PDL=0, read once per process, hence the
+    child processes) gives the same steps, to the summation order of the
+    LoRA gradient atomics."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    import torch
+
+    root = str(Path(__file__).resolve().parent.parent)
+    runs = []
+    for pdl in ("1", "0"):
+        out = tmp_path / f"pdl{pdl}.pt"
+        res = subprocess.run([sys.executable, "-c", _PDL_SCRIPT, root, str(out)],
+                             capture_output=True, text=True, timeout=600,
+                             env={**os.environ, "TQ_PDL": pdl})
+        assert res.returncode == 0, res.stderr[-2000:]
+        runs.append(torch.load(out))
+    a, b = runs
+    assert all(abs(x - y) <= 1e-5 * abs(x) for x, y in zip(a["losses"], b["losses"])), \
+        (a["losses"], b["losses"])
+    assert torch.allclose(a["params"], b["params"], rtol=0, atol=1e-5)
