@@ -376,7 +376,14 @@ def test_accumulate_equals_a_separate_add(cuda, oracle, case):
     if with_bias:
         kw["bias"] = torch.randn(n_out, device=cuda).bfloat16()
     y0 = torch.randn(m, n_out, device=cuda).bfloat16()
-    want = y0.clone().add_(tq.qlora_matmul(x, c, s, b, transpose, 64, 4, **kw))
+    # The result as the accumulating entry point computes it (into zeros: the
+    # small-token kernel, which never accumulates, may differ in the last bit).
+    plain = tq.qlora_matmul(x, c, s, b, transpose, 64, 4, **kw)
+    alone = tq.qlora_matmul(x, c, s, b, transpose, 64, 4,
+                            accumulate=torch.zeros_like(plain), **kw)
+    assert ((alone.float() - plain.float()).abs().max()
+            / plain.float().abs().max()).item() <= TOL
+    want = y0.clone().add_(alone)
     if misaligned:
         buf = torch.empty(m * n_out + 1, dtype=torch.bfloat16, device=cuda)
         acc = buf[1:].view(m, n_out)
@@ -412,3 +419,49 @@ def test_accumulate_argument_errors(cuda):
     with pytest.raises(ValueError, match="accumulate"):
         tq.qlora_matmul(x, c, s, b, accumulate=torch.zeros((4, 128), dtype=torch.float32,
                                                            device=cuda))
+
+
+@pytest.mark.gpu
+def test_quantized_matmul_random_shapes(cuda):
+    """Seeded random shapes across every plan -- the small-token kernel,
+    single CTAs with and without split-K, CTA pairs with ragged token and
+    weight tiles, scale rows that are or are not 16-byte aligned -- forward
+    and dX, 4- and 8-bit, every group size, plain and accumulating, against
+    the exactly dequantized weight in f32."""
+    import random
+
+    import torch
+    import torobi_b200 as tq
+
+    rnd = random.Random(1202)
+    for trial in range(24):
+        bits = rnd.choice((4, 8))
+        group = rnd.choice((32, 64, 128))
+        m = rnd.choice((rnd.randint(1, 40), rnd.randint(41, 700), rnd.randint(701, 3000)))
+        n = 8 * rnd.randint(1, 512)
+        k = group * rnd.randint(1, max(1, 4096 // group))
+        transpose = rnd.random() < 0.5
+        g = torch.Generator(device=cuda)
+        g.manual_seed(trial)
+        w = (torch.randn(n, k, device=cuda, generator=g) * 0.02).bfloat16()
+        c, s, b = tq.quantize(w, group, bits)
+        wd = tq.dequantize(c, s, b, group, bits).float()
+        k_in = k if transpose else n
+        x = torch.randn(m, k_in, device=cuda, generator=g).bfloat16()
+        ref = x.float() @ (wd.t() if transpose else wd)
+        y = tq.quantized_matmul(x, c, s, b, transpose, group, bits)
+        case = (m, n, k, bits, group, transpose)
+        assert torch.isfinite(y.float()).all(), case
+        err = ((y.float() - ref).abs().max() / ref.abs().max().clamp_min(1e-6)).item()
+        assert err <= TOL, (case, err)
+        if trial % 3 == 0:
+            # Accumulating into zeros gives the result itself (the small-token
+            # kernel, which never accumulates, may differ from it in the last
+            # bit); into y0 it gives y0 plus that, as a bf16 add would.
+            y0 = torch.randn(y.shape, device=cuda, generator=g).bfloat16()
+            base = tq.qlora_matmul(x, c, s, b, transpose, group, bits,
+                                   accumulate=torch.zeros_like(y0))
+            err = ((base.float() - ref).abs().max() / ref.abs().max().clamp_min(1e-6)).item()
+            assert err <= TOL, (case, err)
+            acc = tq.qlora_matmul(x, c, s, b, transpose, group, bits, accumulate=y0.clone())
+            assert torch.equal(acc, y0.clone().add_(base)), case
