@@ -291,12 +291,14 @@ cfg = tiny_config(vocab=4096, hidden=1024, intermediate=2816, heads=8, kv_heads=
                                 "up_proj", "down_proj"))
 g = torch.Generator(device=cuda).manual_seed(5)
 batches = [torch.randint(0, cfg.vocab, (4, 512), device=cuda, generator=g) for _ in range(3)]
-model = QLoRACausalLM(cfg, device=cuda, seed=13)
+# The native attention: its backward is deterministic, as every other kernel
+# of the step but the adapter gradients' atomics.
+model = QLoRACausalLM(cfg, device=cuda, seed=13, attention="native")
 tr = Trainer(model, AdamWConfig(lr=1e-3), micro_batch=2)
 # Losses and adapter gradients of two batches on the initial adapters (with
 # B nonzero so every branch carries signal), then one optimizer step.
 with torch.no_grad():
-    model.store.params.normal_(0.0, 0.02)
+    model.store.params.normal_(0.0, 0.02, generator=torch.Generator(device=cuda).manual_seed(6))
 model.store.refresh_bf16(full=True)
 out = {"losses": [], "grads": []}
 for b in batches[:2]:
@@ -339,5 +341,6 @@ def test_steps_match_without_programmatic_dependent_launch(tmp_path):
     # show as errors of the order of the values themselves).
     assert a["losses"] == b["losses"], (a["losses"], b["losses"])
     for ga, gb in zip(a["grads"], b["grads"]):
-        assert ((ga - gb).norm() / ga.norm()).item() < 1e-4
+        assert ((ga - gb).norm() / ga.norm()).item() < 1e-5
     assert abs(a["step_loss"] - b["step_loss"]) <= 1e-5 * abs(a["step_loss"])
+
