@@ -45,10 +45,12 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 
 # DRAM bytes (read + write) per quantized-GEMM launch of the step, from one
 # ncu capture of the 2-layer step (dram__bytes_read.sum + dram__bytes_write.sum
-# per launch: forward 219.2 MB, dX 284.9 MB on average), weighted to the
-# 32-layer step's launch mix (1792 forward, 1768 dX launches).
+# per launch: forward 219.3 MB, dX 305.7 MB on average -- the dX launches of
+# the members after the first of q/k/v and gate/up add into their output in
+# the epilogue, reading it back), weighted to the 32-layer step's launch mix
+# (1792 forward, 1768 dX launches).
 # A constant: it is only as current as the kernel it was captured on.
-QMM_TRAFFIC_PER_LAUNCH = {"llama3-8b": 251.8e6}
+QMM_TRAFFIC_PER_LAUNCH = {"llama3-8b": 262.2e6}
 
 
 def parse_args():
