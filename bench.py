@@ -44,13 +44,14 @@ METRIC = "QLoRA train tokens/s at 1/2/4/8 B200; int4 qmatmul TFLOP/s and % of ro
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 # DRAM bytes (read + write) per quantized-GEMM launch of the step, from one
-# ncu capture of the 2-layer step (dram__bytes_read.sum + dram__bytes_write.sum
-# per launch: forward 219.3 MB, dX 305.7 MB on average -- the dX launches of
-# the members after the first of q/k/v and gate/up add into their output in
-# the epilogue, reading it back), weighted to the 32-layer step's launch mix
-# (1792 forward, 1768 dX launches).
-# A constant: it is only as current as the kernel it was captured on.
-QMM_TRAFFIC_PER_LAUNCH = {"llama3-8b": 262.2e6}
+# ncu capture of the 2-layer step at the default micro-batch of 8 sequences
+# (dram__bytes_read.sum + dram__bytes_write.sum per launch: forward 451.3 MB,
+# dX 636.9 MB on average -- the dX launches of the members after the first of
+# q/k/v and gate/up add into their output in the epilogue, reading it back),
+# weighted to the 32-layer step's launch mix (896 forward, 884 dX launches).
+# A constant: it is only as current as the kernel and micro-batch it was
+# captured on.
+QMM_TRAFFIC_PER_LAUNCH = {"llama3-8b": 543.5e6}
 
 
 def parse_args():
