@@ -104,6 +104,30 @@ def test_quantize_half_integer_quotients_bit_exact(cuda, oracle, bits, group):
     _check_quantize(tq, oracle, _half_integer_matrix(oracle, bits, 512, rng), bits, group, cuda)
 
 
+def _wide_range_matrix(oracle, cols, rng):
+    """Finite groups across the whole bf16 range: N(0, 1) rows scaled by 2^k
+    from subnormal to near the largest finite value (the large ones take the
+    kernel's division path), and rows of random finite bf16 bit patterns,
+    whose groups mix every exponent."""
+    f = np.float32
+    rows = [oracle.bf16_from_f32(rng.standard_normal(cols).astype(f) * f(2.0) ** k)
+            for k in range(-135, 124, 7)]
+    pat = rng.integers(0, 0x10000, size=(16, cols), dtype=np.uint32).astype(np.uint16)
+    finite = (pat & 0x7F80) != 0x7F80
+    rows.append(np.where(finite, pat, np.uint16(0x3F80)).reshape(16, cols))
+    return np.concatenate([np.stack(rows[:-1]), rows[-1]])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("group", [32, 64, 128])
+def test_quantize_wide_range_bit_exact(cuda, oracle, bits, group):
+    import torobi_b200 as tq
+
+    rng = np.random.default_rng(90 + bits + group)
+    _check_quantize(tq, oracle, _wide_range_matrix(oracle, 1024, rng), bits, group, cuda)
+
+
 @pytest.mark.gpu
 def test_quantize_ragged_and_tiny_shapes(cuda, oracle):
     import torobi_b200 as tq

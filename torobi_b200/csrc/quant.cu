@@ -2,10 +2,10 @@
 //
 // Both are HBM-bound streams: quantize reads 2 bytes per element and writes
 // bits/8 + 4/group_size; dequantize the reverse.  Each thread owns whole
-// 16-byte vectors so every global access is a 128-bit transaction, and a
-// group's min/max is reduced across the group_size/32 lanes that hold it with
-// warp shuffles (groups never straddle a warp: 32 lanes x 32 elements covers
-// a whole number of groups for group_size in {32, 64, 128}).
+// 16-byte vectors so every global access is a 128-bit transaction.  A
+// quantizing lane holds 32 or 64 consecutive elements; a group's max and min
+// are exchanged by shuffles among the lanes that hold it (groups never
+// straddle a warp).
 #include <cuda_bf16.h>
 
 #include <cstdio>
@@ -40,48 +40,57 @@ __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
   return static_cast<uint16_t>((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
 }
 
-// Quantizes 32 consecutive elements (four 16-byte vectors r[0..3]) held by
-// lane `lane` of a warp whose 32 lanes hold 32 consecutive such runs (pi is
-// this run's index).  LANES = lanes per group = group_size / 32 (1, 2 or 4);
-// a group's min/max is reduced across its lanes with shuffles, so every lane
-// of the warp must call this.  Thirty-two elements a thread spread the
-// group's three divisions, which every lane of the group computes, over four
-// times the elements of one vector a thread.
-template <int BITS, int LANES>
-__device__ __forceinline__ void quantize_run(const uint4 (&r)[4], bool live, int64_t pi,
-                                             const uint16_t* __restrict__ src,
-                                             int lane, uint32_t* __restrict__ codes,
-                                             uint16_t* __restrict__ scales,
-                                             uint16_t* __restrict__ biases) {
-  constexpr int kE = 32;
+// sat(RN(a * b + c)): one rounding, then clamped to [0, 1] (NaN -> +0).
+__device__ __forceinline__ float fma_rn_sat(float a, float b, float c) {
+  float d;
+  asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// sum over the codes of one word of (bits of 1.5 * 2^23) << (BITS * i), mod 2^32.
+template <int BITS>
+__host__ __device__ constexpr uint32_t round_bits_sum() {
+  uint32_t s = 0;
+  for (int i = 0; i < 32 / BITS; ++i) s += 0x4B400000u << (BITS * i);
+  return s;
+}
+
+// The division path for one run of 32 elements at src (a group whose
+// quotients may be large, infinite or NaN): code = min(rint(fl(d / scale)),
+// 2^BITS - 1) element by element, the conversion rounding to nearest even and
+// saturating (negatives and NaN give 0); the run's code words go straight to
+// out.  Kept out of line so that the rare call leaves the caller's registers
+// to the common path.
+template <int BITS>
+__device__ __noinline__ void quantize_run_exact(const uint16_t* __restrict__ src, float bias,
+                                                float scale, uint32_t* __restrict__ out) {
+  constexpr int kPer = 32 / BITS;
+  constexpr uint32_t kMaxCode = (1u << BITS) - 1u;
+  for (int k = 0; k < BITS; ++k) {
+    uint32_t word = 0;
+    for (int i = 0; i < kPer; ++i) {
+      const float vj = bf16_bits_to_f32(__ldg(src + k * kPer + i));
+      const float yq = __fdiv_rn(__fsub_rn(vj, bias), scale);
+      word |= min(__float2uint_rn(yq), kMaxCode) << (BITS * i);
+    }
+    out[k] = word;
+  }
+}
+
+// A group's scale, bias and reciprocal, and whether its codes may take the
+// division-free path below.
+struct GroupParams {
+  float scale, bias, rs;
+  bool fast;
+};
+
+// MLX's affine group parameters from the group's max and min (f32, exact
+// IEEE divisions as the oracle takes them).  live = false (a run past the end
+// of the matrix) gives fast = true so the dead lane never divides.
+template <int BITS>
+__device__ __forceinline__ GroupParams group_params(float w_max, float w_min, bool live) {
   constexpr float n_bins = static_cast<float>((1 << BITS) - 1);
   constexpr float eps = 1e-7f;
-  uint32_t words[16];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    words[4 * k] = r[k].x;
-    words[4 * k + 1] = r[k].y;
-    words[4 * k + 2] = r[k].z;
-    words[4 * k + 3] = r[k].w;
-  }
-  // Group max/min on bf16 pairs: exact (the result is one of the inputs), a
-  // NaN element is passed over as the f32 comparisons of the oracle do, and
-  // the sign of a zero extreme cannot change the scale or bias below.
-  uint32_t mx2 = 0xFF80FF80u, mn2 = 0x7F807F80u;  // (-inf, -inf), (+inf, +inf)
-  if (live) {
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      mx2 = bf16x2_max(mx2, words[j]);
-      mn2 = bf16x2_min(mn2, words[j]);
-    }
-  }
-  float w_max = fmaxf(bf16_bits_to_f32(mx2 & 0xFFFFu), bf16_bits_to_f32(mx2 >> 16));
-  float w_min = fminf(bf16_bits_to_f32(mn2 & 0xFFFFu), bf16_bits_to_f32(mn2 >> 16));
-#pragma unroll
-  for (int off = 1; off < LANES; off <<= 1) {
-    w_max = mlx_max(w_max, __shfl_xor_sync(0xffffffffu, w_max, off));
-    w_min = mlx_min(w_min, __shfl_xor_sync(0xffffffffu, w_min, off));
-  }
   const bool side = fabsf(w_min) > fabsf(w_max);
   float scale = mlx_max(__fdiv_rn(__fsub_rn(w_max, w_min), n_bins), eps);
   scale = side ? scale : -scale;
@@ -92,115 +101,159 @@ __device__ __forceinline__ void quantize_run(const uint4 (&r)[4], bool live, int
     scale = __fdiv_rn(edge, q0);
     bias = edge;
   }
-  // q = rint(fl((v - bias) / scale)) without a division per element.  With
-  // rs = fl(1 / scale) and y = fl(d * rs), |y - fl(d / scale)| is at most
-  // 1.5 * 2^-23 * |d / scale|: below 2^-14 * 0.75 while |y| < 512, and the
-  // codes of a group keep |y| near [0, 2^bits - 1].  So rint(y) is the
-  // answer unless y lies within 2^-12 of a half-integer (where the rounding
-  // of the quotient itself decides), is not finite, or is that large.  Of
-  // those, an exact quotient (d - y * scale == 0 by one fma, d normal) is y
-  // itself; the rest, about 0.05-0.2 % of elements, take the IEEE division.
-  //
-  // |y| < 512 holds for every element of the group when it holds for the
-  // largest |d| (rounding is monotone, so no element's y exceeds
-  // fl(max|d| * |rs|)); one test a group replaces one an element.  Groups
-  // with an infinite or NaN extreme, or a huge q0, fail it and take the
-  // exact path throughout.
-  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-  constexpr int kMaxCode = (1 << BITS) - 1;
-  const float rs = __frcp_rn(scale);
+  GroupParams g;
+  g.scale = scale;
+  g.bias = bias;
+  g.rs = __frcp_rn(scale);
+  // The division-free path needs every intermediate normal and finite: the
+  // group's quotients below 512 (one test a group: rounding is monotone, so
+  // no element's quotient exceeds fl(max|d| * |rs|)) and |scale| below 2^100
+  // (it is at least 5e-8 for any finite group: the 1e-7 floor, at most
+  // halved by the edge's rounding to q0).  Groups with an infinite or NaN
+  // extreme, or larger ones, divide element by element instead.
   const float d_top = fmaxf(fabsf(__fsub_rn(w_max, bias)), fabsf(__fsub_rn(w_min, bias)));
-  const bool in_range = __fmul_rn(d_top, fabsf(rs)) < 512.0f;
-  uint32_t packed[BITS] = {};  // 32 codes: 4 words at 4 bits, 8 at 8
-  if constexpr (BITS == 4) {
-    // Without a branch or a conversion instruction: t = y + 1.5 * 2^23
-    // rounds y to an integer (ties to even, |y| < 2^22), so t - 1.5 * 2^23
-    // is rint(y) and t's low mantissa bits are that integer; the code is it
-    // clamped to [0, 15].  Elements needing more are marked in `fix` and
-    // redone after the loop from their bf16 value (an L1 hit).
-    uint32_t fix = 0;
+  g.fast = !live || (__fmul_rn(d_top, fabsf(g.rs)) < 512.0f && fabsf(scale) < 0x1p100f);
+  return g;
+}
+
+// Max / min over the bf16 pairs words[0..NW): exact (the result is one of the
+// inputs), a NaN element is passed over as the f32 comparisons of the oracle
+// do, and the sign of a zero extreme cannot change the scale or bias.
+template <int NW>
+__device__ __forceinline__ void pair_max_min(const uint32_t* words, bool live, float& w_max,
+                                             float& w_min) {
+  uint32_t mx2 = 0xFF80FF80u, mn2 = 0x7F807F80u;  // (-inf, -inf), (+inf, +inf)
+  if (live) {
 #pragma unroll
-    for (int j = 0; j < kE; ++j) {
-      const uint32_t h = words[j >> 1];
-      const float vj = (j & 1) ? __uint_as_float(h & 0xFFFF0000u) : __uint_as_float(h << 16);
-      const float d = __fsub_rn(vj, bias);
-      const float y = __fmul_rn(d, rs);
-      const float t = __fadd_rn(y, kRound);
-      const float q = __fsub_rn(t, kRound);
-      if (!(fabsf(__fsub_rn(y, q)) < 0.5f - 0x1p-12f)) fix |= 1u << j;
-      const int qi = static_cast<int>(__float_as_uint(t) - __float_as_uint(kRound));
-      packed[j >> 3] += static_cast<uint32_t>(__vimin_s32_relu(qi, kMaxCode)) << (4 * (j & 7));
-    }
-    if (!in_range) fix = 0xFFFFFFFFu;
-    if (!live) fix = 0;  // src is only valid for a live run
-    while (fix) {
-      const int j = __ffs(fix) - 1;
-      fix &= fix - 1;
-      const float vj = bf16_bits_to_f32(__ldg(src + j));
-      const float d = __fsub_rn(vj, bias);
-      const float y = __fmul_rn(d, rs);
-      const bool exact =
-          fabsf(y) < 512.0f && fabsf(d) > 0x1p-100f && __fmaf_rn(-y, scale, d) == 0.0f;
-      const float yq = exact ? y : __fdiv_rn(d, scale);
-      const uint32_t code = min(__float2uint_rn(yq), static_cast<uint32_t>(kMaxCode));
-      const int sh = 4 * (j & 7);
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-        if (k == (j >> 3)) packed[k] = (packed[k] & ~(15u << sh)) | (code << sh);
-    }
-  } else {
-    // At 8 bits the bf16 grid often puts quotients exactly on half-integers
-    // (about one code per representable value), so the exceptions are
-    // handled in line: a deferred pass over them ran 13-19 % slower here.
-    // The code is the quotient converted with round-to-nearest-even and
-    // saturation (negatives and NaN give 0), capped at 255.
-#pragma unroll
-    for (int j = 0; j < kE; ++j) {
-      const uint32_t h = words[j >> 1];
-      const float vj = (j & 1) ? __uint_as_float(h & 0xFFFF0000u) : __uint_as_float(h << 16);
-      const float d = __fsub_rn(vj, bias);
-      const float y = __fmul_rn(d, rs);
-      float yq = y;
-      if (!(fabsf(__fsub_rn(y, rintf(y))) < 0.5f - 0x1p-12f) || !in_range) {
-        const bool exact = fabsf(y) < 512.0f && fabsf(d) > 0x1p-100f &&
-                           __fmaf_rn(-y, scale, d) == 0.0f;
-        if (!exact) yq = __fdiv_rn(d, scale);
-      }
-      const uint32_t code = min(__float2uint_rn(yq), static_cast<uint32_t>(kMaxCode));
-      packed[j >> 2] += code << (8 * (j & 3));
+    for (int j = 0; j < NW; ++j) {
+      mx2 = bf16x2_max(mx2, words[j]);
+      mn2 = bf16x2_min(mn2, words[j]);
     }
   }
-  if (live) {
-    uint4* out = reinterpret_cast<uint4*>(codes) + pi * (BITS / 4);
-    out[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-    if constexpr (BITS == 8) out[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-    if ((lane & (LANES - 1)) == 0) {
-      const int64_t gi = pi / LANES;
-      scales[gi] = f32_to_bf16_bits(scale);
-      biases[gi] = f32_to_bf16_bits(bias);
-    }
+  w_max = fmaxf(bf16_bits_to_f32(mx2 & 0xFFFFu), bf16_bits_to_f32(mx2 >> 16));
+  w_min = fminf(bf16_bits_to_f32(mn2 & 0xFFFFu), bf16_bits_to_f32(mn2 >> 16));
+}
+
+// The codes of the 2 * NW bf16 elements in words[0..NW) (element 2i in the
+// low half of word i), packed low bits first into packed[0 .. 2 * NW * BITS
+// / 32): code = min(rint(fl(d / scale)), 2^BITS - 1), d = fl(v - bias),
+// without a division and without a branch per element.
+//
+// With rs = fl(1 / scale), P = 2^BITS (the scalings by P are exact),
+// q = fl(d * rs / P) and the residual r = fma(-q, scale * P, d), the corrected
+// quotient fl(q + r * rs / P) is Markstein's refinement of a quotient from a
+// correctly rounded reciprocal (P. Markstein, "Computation of elementary
+// functions on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1),
+// 1990).  Only the integer it rounds to matters here, and over every group
+// this quantizer can form -- each bf16 edge mantissa, each q0, both signs,
+// every bf16 element whose quotient lies in (-1, P + 1), and sampled groups
+// with q0 = 0 -- that integer equals the one from the IEEE quotient, exact
+// half-integer quotients included (checked exhaustively in an exact CPU
+// emulation of these roundings).  The refinement's fma carries .sat, which
+// clamps the quotient / P to [0, 1] and maps a NaN element to code 0;
+// fma(u, P, 1.5 * 2^23) rounds P * u to an integer (ties to even) in its low
+// mantissa bits, and an integer min caps the one value, P, that lies above
+// the top code.  A packed word is sum(t_i << (BITS * i)) minus the same sum
+// of the constant's bits, mod 2^32.
+template <int BITS, int NW>
+__device__ __forceinline__ void quantize_words(const uint32_t* words, const GroupParams& g,
+                                               uint32_t* packed) {
+  constexpr int kPer = 32 / BITS;                // codes per packed word
+  constexpr float kP = static_cast<float>(1 << BITS);
+  constexpr float kRound = 12582912.0f;          // 1.5 * 2^23
+  constexpr uint32_t kRoundBits = 0x4B400000u;   // its bits
+  constexpr uint32_t kTop = kRoundBits + (1u << BITS) - 1u;
+  const float rs_p = __fmul_rn(g.rs, 1.0f / kP);
+  const float scale_p = __fmul_rn(g.scale, kP);
+  const float bias = g.bias;
+#pragma unroll
+  for (int k = 0; k < 2 * NW / kPer; ++k) packed[k] = 0u - round_bits_sum<BITS>();
+#pragma unroll
+  for (int j = 0; j < 2 * NW; ++j) {
+    const uint32_t h = words[j >> 1];
+    const float vj = (j & 1) ? __uint_as_float(h & 0xFFFF0000u) : __uint_as_float(h << 16);
+    const float d = __fsub_rn(vj, bias);
+    const float q = __fmul_rn(d, rs_p);
+    const float res = __fmaf_rn(-q, scale_p, d);
+    const float u = fma_rn_sat(res, rs_p, q);
+    const float t = __fmaf_rn(u, kP, kRound);
+    packed[j / kPer] += min(__float_as_uint(t), kTop) << (BITS * (j % kPer));
   }
 }
 
-// Each warp takes 32 consecutive runs of 32 elements per iteration; the four
-// loads of a thread's run are in flight before it works on any.
-template <int BITS, int LANES>
-__global__ void __launch_bounds__(256) quantize_kernel(const uint4* __restrict__ w,
-                                                       int64_t n_runs, uint32_t* __restrict__ codes,
-                                                       uint16_t* __restrict__ scales,
-                                                       uint16_t* __restrict__ biases) {
+// Quantizes runs RPL * unit .. RPL * unit + RPL - 1 (a run is 32 elements,
+// four 16-byte vectors) for lane `lane` of a warp whose lanes take 32
+// consecutive units.  A group spans LPG = GROUP / (32 * RPL) lanes (1, 2 or
+// 4), whose max and min are exchanged by shuffles, so every lane of the warp
+// must call this.  One lane's group parameters -- three divisions and a
+// reciprocal -- serve its 32 * RPL elements.
+template <int BITS, int GROUP, int RPL>
+__device__ __forceinline__ void quantize_unit(const uint4* __restrict__ w, int64_t n_runs,
+                                              int64_t unit, int lane,
+                                              uint32_t* __restrict__ codes,
+                                              uint16_t* __restrict__ scales,
+                                              uint16_t* __restrict__ biases) {
+  constexpr int NW = 16 * RPL;  // bf16 pairs a lane
+  constexpr int LPG = GROUP / (32 * RPL);
+  static_assert(LPG >= 1 && LPG <= 4, "a group spans one, two or four lanes");
+  const int64_t r0 = RPL * unit;
+  // n_runs is a multiple of GROUP / 32, so the runs of a unit, and the units
+  // of a group, live or die together.
+  const bool live = r0 < n_runs;
+  uint4 v[4 * RPL];
+#pragma unroll
+  for (int k = 0; k < 4 * RPL; ++k) v[k] = live ? __ldg(w + 4 * r0 + k) : make_uint4(0, 0, 0, 0);
+  uint32_t words[NW];
+#pragma unroll
+  for (int k = 0; k < 4 * RPL; ++k) {
+    words[4 * k] = v[k].x;
+    words[4 * k + 1] = v[k].y;
+    words[4 * k + 2] = v[k].z;
+    words[4 * k + 3] = v[k].w;
+  }
+  float w_max, w_min;
+  pair_max_min<NW>(words, live, w_max, w_min);
+#pragma unroll
+  for (int off = 1; off < LPG; off <<= 1) {
+    w_max = mlx_max(w_max, __shfl_xor_sync(0xffffffffu, w_max, off));
+    w_min = mlx_min(w_min, __shfl_xor_sync(0xffffffffu, w_min, off));
+  }
+  const GroupParams g = group_params<BITS>(w_max, w_min, live);
+  uint32_t* out = codes + r0 * BITS;  // BITS code words a run
+  if (g.fast) {
+    uint32_t packed[RPL * BITS];
+    quantize_words<BITS, NW>(words, g, packed);
+    if (live) {
+#pragma unroll
+      for (int k = 0; k < RPL * BITS / 4; ++k)
+        reinterpret_cast<uint4*>(out)[k] =
+            make_uint4(packed[4 * k], packed[4 * k + 1], packed[4 * k + 2], packed[4 * k + 3]);
+    }
+  } else {
+    const uint16_t* src = reinterpret_cast<const uint16_t*>(w + 4 * r0);
+#pragma unroll
+    for (int r = 0; r < RPL; ++r)
+      quantize_run_exact<BITS>(src + 32 * r, g.bias, g.scale, out + BITS * r);
+  }
+  if (live && (lane & (LPG - 1)) == 0) {
+    const int64_t gi = r0 * 32 / GROUP;
+    scales[gi] = f32_to_bf16_bits(g.scale);
+    biases[gi] = f32_to_bf16_bits(g.bias);
+  }
+}
+
+// One matrix: a run a lane (47 registers a thread, five CTAs an SM), so a
+// short launch spreads over many CTAs.  Each warp takes 32 consecutive runs
+// per iteration; the loads of a lane are in flight before it works on any.
+template <int BITS, int GROUP>
+__global__ void __launch_bounds__(256, 5)
+    quantize_kernel(const uint4* __restrict__ w, int64_t n_runs, uint32_t* __restrict__ codes,
+                    uint16_t* __restrict__ scales, uint16_t* __restrict__ biases) {
   const int lane = threadIdx.x & 31;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31);
-       base < n_runs; base += stride) {
-    const int64_t pi = base + lane;
-    const bool live = pi < n_runs;
-    uint4 r[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) r[k] = live ? __ldg(w + 4 * pi + k) : make_uint4(0, 0, 0, 0);
-    quantize_run<BITS, LANES>(r, live, pi, reinterpret_cast<const uint16_t*>(w + 4 * pi), lane,
-                              codes, scales, biases);
-  }
+       base < n_runs; base += stride)
+    quantize_unit<BITS, GROUP, 1>(w, n_runs, base + lane, lane, codes, scales, biases);
 }
 
 // One code word a lane per step (8 elements at 4 bits, 4 at 8), so a warp
@@ -301,22 +354,25 @@ __device__ __forceinline__ int find_job(const int64_t* start, int n, int64_t v) 
   return lo;
 }
 
-template <int BITS, int LANES>
-__global__ void __launch_bounds__(256) quantize_batch_kernel(const __grid_constant__ QuantizeBatch b) {
+// Runs a lane of the batched quantize: one at groups of 32, two at 64 and 128
+// (one lane's group parameters then serve 64 elements; 64 registers a thread,
+// four CTAs an SM).  Over a whole model's matrices this measured faster than
+// a run a lane at 64 and 128, and slower at 32.
+template <int GROUP>
+constexpr int batch_runs_per_lane() { return GROUP == 32 ? 1 : 2; }
+
+template <int BITS, int GROUP>
+__global__ void __launch_bounds__(256, GROUP == 32 ? 5 : 4)
+    quantize_batch_kernel(const __grid_constant__ QuantizeBatch b) {
+  constexpr int RPL = batch_runs_per_lane<GROUP>();
   const int lane = threadIdx.x & 31;
-  const int64_t end = b.start[b.n];
+  const int64_t end = b.start[b.n] / RPL;  // in units
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31);
        base < end; base += stride) {
-    const int j = find_job(b.start, b.n, base);
-    const int64_t pi = base - b.start[j] + lane;
-    const bool live = pi < b.runs[j];
-    const uint4* w = b.w[j];
-    uint4 r[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) r[k] = live ? __ldg(w + 4 * pi + k) : make_uint4(0, 0, 0, 0);
-    quantize_run<BITS, LANES>(r, live, pi, reinterpret_cast<const uint16_t*>(w + 4 * pi), lane,
-                              b.codes[j], b.scales[j], b.biases[j]);
+    const int j = find_job(b.start, b.n, RPL * base);
+    quantize_unit<BITS, GROUP, RPL>(b.w[j], b.runs[j], base - b.start[j] / RPL + lane, lane,
+                                    b.codes[j], b.scales[j], b.biases[j]);
   }
 }
 
@@ -355,6 +411,18 @@ int grid_for(int64_t work_items, int block) {
   return static_cast<int>(want < 1 ? 1 : (want > cap ? cap : want));
 }
 
+template <int BITS, int GROUP>
+void launch_quantize(const uint4* w, int64_t n_runs, uint32_t* c, uint16_t* sc, uint16_t* bi,
+                     cudaStream_t s) {
+  quantize_kernel<BITS, GROUP><<<grid_for(n_runs, 256), 256, 0, s>>>(w, n_runs, c, sc, bi);
+}
+
+template <int BITS, int GROUP>
+void launch_quantize_batch(const QuantizeBatch& b, cudaStream_t s) {
+  const int grid = grid_for(b.start[b.n] / batch_runs_per_lane<GROUP>(), 256);
+  quantize_batch_kernel<BITS, GROUP><<<grid, 256, 0, s>>>(b);
+}
+
 }  // namespace
 }  // namespace tq
 
@@ -370,22 +438,19 @@ extern "C" int tq_quantize(const void* w, int64_t rows, int64_t cols, int group_
   if (!aligned(scales, 2) || !aligned(biases, 2))
     return fail(TQ_ERR_MISALIGNED, "scales and biases must be 2-byte aligned");
   const int64_t n_runs = rows * cols / 32;  // cols % 32 == 0
-  const int block = 256;
-  const int grid = grid_for(n_runs, block);
   cudaStream_t s = as_stream(stream);
   const uint4* wv = static_cast<const uint4*>(w);
   uint32_t* c = static_cast<uint32_t*>(codes);
   uint16_t* sc = static_cast<uint16_t*>(scales);
   uint16_t* bi = static_cast<uint16_t*>(biases);
-  const int lanes = group_size / 32;
   if (bits == 4) {
-    if (lanes == 1) quantize_kernel<4, 1><<<grid, block, 0, s>>>(wv, n_runs, c, sc, bi);
-    else if (lanes == 2) quantize_kernel<4, 2><<<grid, block, 0, s>>>(wv, n_runs, c, sc, bi);
-    else quantize_kernel<4, 4><<<grid, block, 0, s>>>(wv, n_runs, c, sc, bi);
+    if (group_size == 32) launch_quantize<4, 32>(wv, n_runs, c, sc, bi, s);
+    else if (group_size == 64) launch_quantize<4, 64>(wv, n_runs, c, sc, bi, s);
+    else launch_quantize<4, 128>(wv, n_runs, c, sc, bi, s);
   } else {
-    if (lanes == 1) quantize_kernel<8, 1><<<grid, block, 0, s>>>(wv, n_runs, c, sc, bi);
-    else if (lanes == 2) quantize_kernel<8, 2><<<grid, block, 0, s>>>(wv, n_runs, c, sc, bi);
-    else quantize_kernel<8, 4><<<grid, block, 0, s>>>(wv, n_runs, c, sc, bi);
+    if (group_size == 32) launch_quantize<8, 32>(wv, n_runs, c, sc, bi, s);
+    else if (group_size == 64) launch_quantize<8, 64>(wv, n_runs, c, sc, bi, s);
+    else launch_quantize<8, 128>(wv, n_runs, c, sc, bi, s);
   }
   return check_cuda(cudaGetLastError(), "quantize launch");
 }
@@ -454,7 +519,6 @@ extern "C" int tq_quantize_batch(const TqQuantizeJob* jobs, int n_jobs, int grou
     if (rc) return rc;
   }
   cudaStream_t s = as_stream(stream);
-  const int lanes = group_size / 32;
   QuantizeBatch b;
   int i = 0;
   while (i < n_jobs) {
@@ -470,20 +534,19 @@ extern "C" int tq_quantize_batch(const TqQuantizeJob* jobs, int n_jobs, int grou
       b.codes[b.n] = static_cast<uint32_t*>(j.codes);
       b.scales[b.n] = static_cast<uint16_t*>(j.scales);
       b.biases[b.n] = static_cast<uint16_t*>(j.biases);
-      v += (runs + 31) / 32 * 32;  // whole warp iterations
+      v += (runs + 63) / 64 * 64;  // whole warp iterations (32 lanes x up to 2 runs)
       ++b.n;
     }
     if (b.n == 0) break;
     b.start[b.n] = v;
-    const int grid = grid_for(v, 256);
     if (bits == 4) {
-      if (lanes == 1) quantize_batch_kernel<4, 1><<<grid, 256, 0, s>>>(b);
-      else if (lanes == 2) quantize_batch_kernel<4, 2><<<grid, 256, 0, s>>>(b);
-      else quantize_batch_kernel<4, 4><<<grid, 256, 0, s>>>(b);
+      if (group_size == 32) launch_quantize_batch<4, 32>(b, s);
+      else if (group_size == 64) launch_quantize_batch<4, 64>(b, s);
+      else launch_quantize_batch<4, 128>(b, s);
     } else {
-      if (lanes == 1) quantize_batch_kernel<8, 1><<<grid, 256, 0, s>>>(b);
-      else if (lanes == 2) quantize_batch_kernel<8, 2><<<grid, 256, 0, s>>>(b);
-      else quantize_batch_kernel<8, 4><<<grid, 256, 0, s>>>(b);
+      if (group_size == 32) launch_quantize_batch<8, 32>(b, s);
+      else if (group_size == 64) launch_quantize_batch<8, 64>(b, s);
+      else launch_quantize_batch<8, 128>(b, s);
     }
     rc = check_cuda(cudaGetLastError(), "quantize_batch launch");
     if (rc) return rc;
