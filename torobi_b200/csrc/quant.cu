@@ -181,42 +181,90 @@ __device__ __forceinline__ void quantize_words(const uint32_t* words, const Grou
   }
 }
 
+// ------------------------------------------------- staged loads (cp.async) --
+//
+// A warp copies its next iteration's 32 units (2 or 4 KB, contiguous) into its
+// shared-memory region with cp.async while it quantizes the current ones, so
+// loads stay in flight without holding registers.  The copy is coalesced
+// (instruction i: lane l takes 16-byte piece 32 i + l, 512 contiguous bytes a
+// warp); each lane then reads its own unit's 4 * RPL pieces.  Pieces are
+// placed so that the eight lanes of a quarter-warp hit eight different
+// 16-byte bank groups, both when they write and when they read.
+
+// Piece k of lane l's unit sits at 16-byte slot 4 * RPL * l + (k ^ f(l)) of
+// the warp region, f(l) = l & 7 at two runs a lane and (l >> 1) & 3 at one.
+template <int RPL>
+__device__ __forceinline__ int slot_xor(int l) { return RPL == 2 ? (l & 7) : ((l >> 1) & 3); }
+
+// Starts the copy of units first .. first + 31 of w (those below n_units)
+// into the warp region wb.  Instruction i of the copy moves piece 32 i + lane
+// of the chunk, which is piece k = lane % (4 RPL) of unit l = 32 i / (4 RPL)
+// + lane / (4 RPL); its slot offset is 512 i plus a per-lane constant (two
+// alternating ones at two runs a lane).  Every lane of the warp calls this
+// after the warp's reads of the region (see stage_read).
+template <int RPL>
+__device__ __forceinline__ void stage_copy(uint32_t wb, int lane, const uint4* w, int64_t first,
+                                           int64_t n_units) {
+  constexpr int P = 4 * RPL;      // pieces a unit
+  constexpr int UI = 32 / P;      // units an instruction covers
+  const int k = lane % P, lu = lane / P;
+  // slot(l, k) - 32 i for l = UI i + lu, even and odd i
+  const uint32_t off_e = wb + 16u * static_cast<uint32_t>(P * lu + (k ^ slot_xor<RPL>(lu)));
+  const uint32_t off_o = wb + 16u * static_cast<uint32_t>(P * lu + (k ^ slot_xor<RPL>(UI + lu)));
+  const uint4* src = w + P * first + lane;
+  const int64_t rem = n_units - first;  // units of the chunk that exist
+  __syncwarp();  // every lane's reads of the region come before any refill
+#pragma unroll
+  for (int i = 0; i < P; ++i) {
+    if (rem >= 32 || UI * i + lu < rem)
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                   ::"r"(((i & 1) ? off_o : off_e) + 512u * i), "l"(src + 32 * i)
+                   : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// Waits for the warp's copies and reads this lane's unit into words.
+template <int RPL>
+__device__ __forceinline__ void stage_read(uint32_t wb, int lane, uint32_t* words) {
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncwarp();  // the other lanes' copies are visible
+  const uint32_t lb = (wb + 64u * RPL * lane) | (16u * slot_xor<RPL>(lane));
+#pragma unroll
+  for (int k = 0; k < 4 * RPL; ++k)
+    lds128(lb ^ (16u * k), words[4 * k], words[4 * k + 1], words[4 * k + 2], words[4 * k + 3]);
+}
+
+// Runs a quantizing lane takes: one at groups of 32 (one group a lane), two
+// at 64 (one group a lane) and 128 (half a group a lane), so one lane's group
+// parameters -- three divisions and a reciprocal -- serve 32 or 64 elements.
+template <int GROUP>
+constexpr int runs_per_lane() { return GROUP == 32 ? 1 : 2; }
+
 // Quantizes runs RPL * unit .. RPL * unit + RPL - 1 (a run is 32 elements,
 // four 16-byte vectors) for lane `lane` of a warp whose lanes take 32
-// consecutive units.  A group spans LPG = GROUP / (32 * RPL) lanes (1, 2 or
-// 4), whose max and min are exchanged by shuffles, so every lane of the warp
-// must call this.  One lane's group parameters -- three divisions and a
-// reciprocal -- serve its 32 * RPL elements.
+// consecutive units, from the words already read; before any other work the
+// warp starts the copy of its next units (from unit next_first of next_w,
+// next_units of them in that matrix) into the region the words came from.  A group spans LPG = GROUP / (32 * RPL) lanes
+// (1 or 2), whose max and min are exchanged by a shuffle, so every lane of the
+// warp must call this.
 template <int BITS, int GROUP, int RPL>
-__device__ __forceinline__ void quantize_unit(const uint4* __restrict__ w, int64_t n_runs,
-                                              int64_t unit, int lane,
+__device__ __forceinline__ void quantize_unit(const uint32_t* words, bool live, int64_t r0,
+                                              int lane, uint32_t wb, const uint4* next_w,
+                                              int64_t next_first, int64_t next_units,
+                                              const uint4* __restrict__ src,
                                               uint32_t* __restrict__ codes,
                                               uint16_t* __restrict__ scales,
                                               uint16_t* __restrict__ biases) {
   constexpr int NW = 16 * RPL;  // bf16 pairs a lane
   constexpr int LPG = GROUP / (32 * RPL);
-  static_assert(LPG >= 1 && LPG <= 4, "a group spans one, two or four lanes");
-  const int64_t r0 = RPL * unit;
-  // n_runs is a multiple of GROUP / 32, so the runs of a unit, and the units
-  // of a group, live or die together.
-  const bool live = r0 < n_runs;
-  uint4 v[4 * RPL];
-#pragma unroll
-  for (int k = 0; k < 4 * RPL; ++k) v[k] = live ? __ldg(w + 4 * r0 + k) : make_uint4(0, 0, 0, 0);
-  uint32_t words[NW];
-#pragma unroll
-  for (int k = 0; k < 4 * RPL; ++k) {
-    words[4 * k] = v[k].x;
-    words[4 * k + 1] = v[k].y;
-    words[4 * k + 2] = v[k].z;
-    words[4 * k + 3] = v[k].w;
-  }
+  static_assert(LPG == 1 || LPG == 2, "a group spans one or two lanes");
   float w_max, w_min;
   pair_max_min<NW>(words, live, w_max, w_min);
-#pragma unroll
-  for (int off = 1; off < LPG; off <<= 1) {
-    w_max = mlx_max(w_max, __shfl_xor_sync(0xffffffffu, w_max, off));
-    w_min = mlx_min(w_min, __shfl_xor_sync(0xffffffffu, w_min, off));
+  stage_copy<RPL>(wb, lane, next_w, next_first, next_units);  // the words are in registers
+  if constexpr (LPG == 2) {
+    w_max = mlx_max(w_max, __shfl_xor_sync(0xffffffffu, w_max, 1));
+    w_min = mlx_min(w_min, __shfl_xor_sync(0xffffffffu, w_min, 1));
   }
   const GroupParams g = group_params<BITS>(w_max, w_min, live);
   uint32_t* out = codes + r0 * BITS;  // BITS code words a run
@@ -230,10 +278,10 @@ __device__ __forceinline__ void quantize_unit(const uint4* __restrict__ w, int64
             make_uint4(packed[4 * k], packed[4 * k + 1], packed[4 * k + 2], packed[4 * k + 3]);
     }
   } else {
-    const uint16_t* src = reinterpret_cast<const uint16_t*>(w + 4 * r0);
+    const uint16_t* e = reinterpret_cast<const uint16_t*>(src + 4 * r0);
 #pragma unroll
     for (int r = 0; r < RPL; ++r)
-      quantize_run_exact<BITS>(src + 32 * r, g.bias, g.scale, out + BITS * r);
+      quantize_run_exact<BITS>(e + 32 * r, g.bias, g.scale, out + BITS * r);
   }
   if (live && (lane & (LPG - 1)) == 0) {
     const int64_t gi = r0 * 32 / GROUP;
@@ -242,18 +290,30 @@ __device__ __forceinline__ void quantize_unit(const uint4* __restrict__ w, int64
   }
 }
 
-// One matrix: a run a lane (47 registers a thread, five CTAs an SM), so a
-// short launch spreads over many CTAs.  Each warp takes 32 consecutive runs
-// per iteration; the loads of a lane are in flight before it works on any.
+// Each warp takes 32 consecutive units per iteration (n_runs is a multiple of
+// GROUP / 32, so a unit's runs live or die together).  A run a lane: 64
+// registers a thread and 16 KB of slots a CTA, four CTAs an SM; two runs: 80
+// registers and 32 KB, three.
 template <int BITS, int GROUP>
-__global__ void __launch_bounds__(256, 5)
+__global__ void __launch_bounds__(256, GROUP == 32 ? 4 : 3)
     quantize_kernel(const uint4* __restrict__ w, int64_t n_runs, uint32_t* __restrict__ codes,
                     uint16_t* __restrict__ scales, uint16_t* __restrict__ biases) {
+  constexpr int RPL = runs_per_lane<GROUP>();
+  __shared__ __align__(128) uint4 region[256 * 4 * RPL];
   const int lane = threadIdx.x & 31;
+  const uint32_t wb = smem_u32(region) + (threadIdx.x & ~31) * (64u * RPL);
+  const int64_t n_units = n_runs / RPL;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31);
-       base < n_runs; base += stride)
-    quantize_unit<BITS, GROUP, 1>(w, n_runs, base + lane, lane, codes, scales, biases);
+  int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31);
+  stage_copy<RPL>(wb, lane, w, base, n_units);
+  for (; base < n_units; base += stride) {
+    const int64_t unit = base + lane;
+    uint32_t words[16 * RPL];
+    stage_read<RPL>(wb, lane, words);
+    quantize_unit<BITS, GROUP, RPL>(words, unit < n_units, RPL * unit, lane, wb, w,
+                                    base + stride, n_units, w, codes, scales, biases);
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");  // no copy outlives the CTA
 }
 
 // One code word a lane per step (8 elements at 4 bits, 4 at 8), so a warp
@@ -354,26 +414,40 @@ __device__ __forceinline__ int find_job(const int64_t* start, int n, int64_t v) 
   return lo;
 }
 
-// Runs a lane of the batched quantize: one at groups of 32, two at 64 and 128
-// (one lane's group parameters then serve 64 elements; 64 registers a thread,
-// four CTAs an SM).  Over a whole model's matrices this measured faster than
-// a run a lane at 64 and 128, and slower at 32.
-template <int GROUP>
-constexpr int batch_runs_per_lane() { return GROUP == 32 ? 1 : 2; }
-
+// The batched form of quantize_kernel: a warp finds its job once per
+// iteration (a job's units never straddle a warp iteration) and the next
+// iteration's job by stepping forward from this one.
+// The batched form of quantize_kernel: a warp finds its job once per
+// iteration (a job's units never straddle a warp iteration) and the next
+// iteration's job by stepping forward from this one.
 template <int BITS, int GROUP>
-__global__ void __launch_bounds__(256, GROUP == 32 ? 5 : 4)
+__global__ void __launch_bounds__(256, GROUP == 32 ? 4 : 3)
     quantize_batch_kernel(const __grid_constant__ QuantizeBatch b) {
-  constexpr int RPL = batch_runs_per_lane<GROUP>();
+  constexpr int RPL = runs_per_lane<GROUP>();
+  __shared__ __align__(128) uint4 region[256 * 4 * RPL];
   const int lane = threadIdx.x & 31;
+  const uint32_t wb = smem_u32(region) + (threadIdx.x & ~31) * (64u * RPL);
   const int64_t end = b.start[b.n] / RPL;  // in units
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31);
-       base < end; base += stride) {
-    const int j = find_job(b.start, b.n, RPL * base);
-    quantize_unit<BITS, GROUP, RPL>(b.w[j], b.runs[j], base - b.start[j] / RPL + lane, lane,
+  int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31);
+  // Job j's units, and the warp's first unit in it, for a warp at virtual unit bs.
+  auto units = [&](int job) { return b.runs[job] / RPL; };
+  auto first = [&](int job, int64_t bs) { return bs - b.start[job] / RPL; };
+  int j = find_job(b.start, b.n, RPL * (base < end ? base : 0));
+  stage_copy<RPL>(wb, lane, b.w[j], first(j, base), base < end ? units(j) : 0);
+  for (; base < end; base += stride) {
+    int jn = j;  // the job of the next iteration
+    const int64_t nb = base + stride;
+    while (jn + 1 < b.n && b.start[jn + 1] <= RPL * nb) ++jn;
+    const int64_t u = first(j, base) + lane;
+    uint32_t words[16 * RPL];
+    stage_read<RPL>(wb, lane, words);
+    quantize_unit<BITS, GROUP, RPL>(words, u < units(j), RPL * u, lane, wb, b.w[jn],
+                                    first(jn, nb), nb < end ? units(jn) : 0, b.w[j],
                                     b.codes[j], b.scales[j], b.biases[j]);
+    j = jn;
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 template <int BITS>
@@ -414,12 +488,13 @@ int grid_for(int64_t work_items, int block) {
 template <int BITS, int GROUP>
 void launch_quantize(const uint4* w, int64_t n_runs, uint32_t* c, uint16_t* sc, uint16_t* bi,
                      cudaStream_t s) {
-  quantize_kernel<BITS, GROUP><<<grid_for(n_runs, 256), 256, 0, s>>>(w, n_runs, c, sc, bi);
+  const int grid = grid_for(n_runs / runs_per_lane<GROUP>(), 256);
+  quantize_kernel<BITS, GROUP><<<grid, 256, 0, s>>>(w, n_runs, c, sc, bi);
 }
 
 template <int BITS, int GROUP>
 void launch_quantize_batch(const QuantizeBatch& b, cudaStream_t s) {
-  const int grid = grid_for(b.start[b.n] / batch_runs_per_lane<GROUP>(), 256);
+  const int grid = grid_for(b.start[b.n] / runs_per_lane<GROUP>(), 256);
   quantize_batch_kernel<BITS, GROUP><<<grid, 256, 0, s>>>(b);
 }
 
