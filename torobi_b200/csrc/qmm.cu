@@ -110,6 +110,7 @@ struct Params {
   float* ws;                 // splits > 1: f32 partials [splits, m, n_out]
   int tma_y;                 // the bf16 output goes out through TMA stores (tm_y)
   int acc;                   // add into y: y = RNE(RNE(result) + y)
+  int keep_weights;          // weight loads marked L2 evict_last (else evict_normal)
   int* status;
 };
 
@@ -400,7 +401,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ producer
     if (elect_one_sync()) {
       tma_prefetch_desc(&tm_x);
-      const uint64_t keep = l2_evict_last();  // codes and scales: reused by every token tile
+      // codes and scales: reused by every token tile
+      const uint64_t keep = p.keep_weights ? l2_evict_last() : l2_evict_normal();
       tma_prefetch_desc(&tm_c);
       if constexpr (STMA) {
         tma_prefetch_desc(&tm_sc);
@@ -980,6 +982,17 @@ int make_maps(const Args& a, int x_rows, int sc_rows, bool stma, Maps& mp) {
   return TQ_OK;
 }
 
+// The packed weight and its scales are loaded with an L2 evict_last policy
+// (every token tile reads them again); TQ_QMM_KEEP=0 loads them at normal
+// priority, for comparison runs.
+int keep_weights() {
+  static const int keep = [] {
+    const char* e = getenv("TQ_QMM_KEEP");
+    return e && e[0] == '0' ? 0 : 1;
+  }();
+  return keep;
+}
+
 Params make_params(const Args& a, const Plan& pl, int tile_rows, int bn, int* status) {
   const int64_t k_red = a.transpose ? a.w_cols : a.w_rows;
   const int64_t n_out = a.transpose ? a.w_rows : a.w_cols;
@@ -1003,6 +1016,7 @@ Params make_params(const Args& a, const Plan& pl, int tile_rows, int bn, int* st
   p.ws = static_cast<float*>(a.ws);
   p.tma_y = 0;
   p.acc = a.acc;
+  p.keep_weights = keep_weights();
   p.status = status;
   return p;
 }

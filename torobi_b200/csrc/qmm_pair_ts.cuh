@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ producer
     if (elect_one_sync()) {
       tma_prefetch_desc(&tm_x);
-      const uint64_t keep = l2_evict_last();
+      const uint64_t keep = p.keep_weights ? l2_evict_last() : l2_evict_normal();
       tma_prefetch_desc(&tm_c);
       tma_prefetch_desc(&tm_sc);
       tma_prefetch_desc(&tm_bi);

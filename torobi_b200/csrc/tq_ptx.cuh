@@ -131,6 +131,13 @@ __device__ __forceinline__ uint64_t l2_evict_last() {
   return p;
 }
 
+// The default L2 priority, as a cache hint for the same loads.
+__device__ __forceinline__ uint64_t l2_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
 __device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const CUtensorMap* map,
                                                  uint32_t bar, int32_t c0, int32_t c1,
                                                  uint64_t policy) {
