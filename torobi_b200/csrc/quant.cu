@@ -245,9 +245,9 @@ constexpr int runs_per_lane() { return GROUP == 32 ? 1 : 2; }
 // four 16-byte vectors) for lane `lane` of a warp whose lanes take 32
 // consecutive units, from the words already read; before any other work the
 // warp starts the copy of its next units (from unit next_first of next_w,
-// next_units of them in that matrix) into the region the words came from.  A group spans LPG = GROUP / (32 * RPL) lanes
-// (1 or 2), whose max and min are exchanged by a shuffle, so every lane of the
-// warp must call this.
+// next_units of them in that matrix) into the region the words came from.
+// A group spans LPG = GROUP / (32 * RPL) lanes (1 or 2), whose max and min
+// are exchanged by a shuffle, so every lane of the warp must call this.
 template <int BITS, int GROUP, int RPL>
 __device__ __forceinline__ void quantize_unit(const uint32_t* words, bool live, int64_t r0,
                                               int lane, uint32_t wb, const uint4* next_w,
